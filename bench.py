@@ -1,0 +1,383 @@
+#!/usr/bin/env python
+"""MoE-layer throughput benchmark (tokens/s) for the B200 execution backend.
+
+Workload (one step = one MoE layer forward over one batch):
+    tokens [8192, 4096] bf16 ~ N(0,1); router W [4096, 64] ~ N(0, 0.02);
+    softmax top-2 over 64 experts; each expert a gated FFN 4096 -> 1408 -> 4096
+    with weights ~ N(0, 0.02); dispatch, grouped GEMM, weighted combine.
+Inputs are synthetic, seeded (torch generator seed 0), generated on the
+device; weights are random-init with the layer's shapes. The working set
+(2.2 GB of expert weights + 0.5 GB of activations per step) is far larger
+than the 126 MB L2, so no flush is needed between timed steps.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+N > 1 runs under torch.distributed (one process per GPU, NCCL): each rank
+holds 8192 tokens (weak scaling) and the experts are sharded over the ranks
+(expert parallel) with an all-to-all exchange of the routed token rows.
+
+--impl reference times the CPU restatement of the layer (the reference
+toolkit itself has no execution path) on this machine's host cores, on a
+bounded token sample per step.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+TOKENS, HIDDEN, EXPERTS, FFN, TOP_K = 8192, 4096, 64, 1408, 2
+METRIC = "MoE-layer tokens/s"
+UNIT = "tokens/s"
+CONFIG_NAME = "moe_layer_T8192_H4096_E64_F1408_top2"
+
+
+def parse_args(argv=None):
+    ap = argparse.ArgumentParser(description=__doc__,
+                                 formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-cpu-baseline", action="store_true",
+                    help="skip the CPU baseline leg (rank 0, N=1)")
+    return ap.parse_args(argv)
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return dict(hbm=d["hbm_gbs"], bf16=d["bf16_tflops"],
+                    bf16_sustained=d["bf16_tflops_sustained"], src="measured")
+    return dict(hbm=6650.0, bf16=1590.0, bf16_sustained=1400.0, src="fallback")
+
+
+# ----------------------------------------------------------- clock sampler ---
+
+class ClockSampler:
+    """Samples nvidia-smi SM clocks and throttle reasons in the background."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu_index = gpu_index
+        self.samples: list[tuple[float, list[str]]] = []
+        self.proc = None
+        self.thread = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                 "-i", str(self.gpu_index), "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except (FileNotFoundError, OSError):
+            self.proc = None
+            return self
+
+        def reader():
+            for line in self.proc.stdout:
+                self.samples.append((time.time(), [x.strip() for x in line.split(",")]))
+        self.thread = threading.Thread(target=reader, daemon=True)
+        self.thread.start()
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+        if self.thread is not None:
+            self.thread.join(timeout=2)
+
+    def summary(self, t0: float, t1: float) -> dict:
+        inside = [s for t, s in self.samples if t0 <= t <= t1]
+        if not inside:   # timed region shorter than the sampling period
+            inside = [s for t, s in self.samples if t0 - 0.25 <= t <= t1 + 0.25]
+        if not inside:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        sm = [float(s[1]) for s in inside if s[1].replace(".", "").isdigit()]
+        mx = [float(s[2]) for s in inside if s[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for s in inside for n, v in zip(names, s[5:9]) if v == "Active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(inside)}
+
+
+# --------------------------------------------------------------- our arm ---
+
+def dist_env():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def make_weights(torch, dev, gen):
+    wr = (torch.randn((EXPERTS, HIDDEN), generator=gen, device=dev) * 0.02).to(torch.bfloat16)
+    w13 = torch.empty((EXPERTS, 2 * FFN, HIDDEN), dtype=torch.bfloat16, device=dev)
+    w2 = torch.empty((EXPERTS, HIDDEN, FFN), dtype=torch.bfloat16, device=dev)
+    for e in range(EXPERTS):   # chunked to bound the fp32 temporaries
+        w13[e] = (torch.randn((2 * FFN, HIDDEN), generator=gen, device=dev) * 0.02)
+        w2[e] = (torch.randn((HIDDEN, FFN), generator=gen, device=dev) * 0.02)
+    return wr, w13, w2
+
+
+def cpu_baseline_leg(x_dev, wr, w13, w2, budget_s: float = 20.0) -> dict:
+    """The oracle (CPU restatement of the layer) on a bounded token sample."""
+    import numpy as np
+    import torch
+    import oracle
+
+    def bits(t):
+        return t.contiguous().view(torch.int16).cpu().numpy().view(np.uint16)
+
+    xs, wrs, w13s, w2s = bits(x_dev[:1024]), bits(wr), bits(w13), bits(w2)
+    oracle.moe_layer(xs[:16], wrs, w13s, w2s, TOP_K)          # warm-up
+    t = time.perf_counter()
+    oracle.moe_layer(xs[:64], wrs, w13s, w2s, TOP_K)
+    per_tok = (time.perf_counter() - t) / 64
+    n = int(max(64, min(1024, budget_s / max(per_tok, 1e-6) / 2)))
+    t = time.perf_counter()
+    oracle.moe_layer(xs[:n], wrs, w13s, w2s, TOP_K)
+    dt = time.perf_counter() - t
+    return {"value": n / dt, "unit": UNIT, "cores": oracle.num_threads(), "kind": "port",
+            "sample": f"first {n} of the 8192 tokens through the whole layer "
+                      f"(same weights), one call, {dt:.2f} s"}
+
+
+def run_ours(args) -> int:
+    import torch
+    import torch.distributed as dist
+
+    world, rank, local = dist_env()
+    if world != args.gpus:
+        print(f"--gpus {args.gpus} but WORLD_SIZE={world}", file=sys.stderr)
+        return 2
+    if not torch.cuda.is_available():
+        print(json.dumps({"metric": METRIC, "error": "no CUDA device"}))
+        return 1
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120),
+                                device_id=dev)
+
+    from kvm_b200 import _lib
+    from kvm_b200.moe import MoELayer
+
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(0)
+    wr, w13, w2 = make_weights(torch, dev, gen)
+    gen.manual_seed(1000 + rank)
+    x = torch.randn((TOKENS, HIDDEN), generator=gen, device=dev).to(torch.bfloat16)
+
+    if world > 1:
+        from kvm_b200.ep import ExpertParallelMoE
+        layer = ExpertParallelMoE(wr, w13, w2, top_k=TOP_K, max_tokens=TOKENS,
+                                  rank=rank, world=world)
+    else:
+        layer = MoELayer(wr, w13, w2, TOP_K, TOKENS)
+    del w13, w2
+    torch.cuda.synchronize()
+
+    stream = torch.cuda.current_stream()
+    probe = {"start": [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)],
+             "end": [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]}
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local])
+
+    # ---- device-resident timing
+    for _ in range(args.warmup):
+        layer(x)
+    _lib.device_status()
+    barrier()
+    torch.cuda.synchronize()
+    ev0 = torch.cuda.Event(enable_timing=True)
+    ev1 = torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        barrier()
+        torch.cuda.synchronize()
+        wall0 = time.time()
+        ev0.record(stream)
+        for i in range(args.steps):
+            layer(x, probe=(probe["start"][i], probe["end"][i]))
+        ev1.record(stream)
+        torch.cuda.synchronize()
+        wall1 = time.time()
+        barrier()
+    _lib.device_status()
+    ms = ev0.elapsed_time(ev1)
+    gemm_ms = statistics.mean(s.elapsed_time(e) for s, e in zip(probe["start"], probe["end"]))
+    if world > 1:
+        t = torch.tensor([ms, gemm_ms], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms, gemm_ms = float(t[0]), float(t[1])
+    ms_per_step = ms / args.steps
+    value = TOKENS * world * args.steps / (ms / 1e3)
+
+    # ---- end to end through the public API: pinned host in, host out
+    x_host = x.cpu().pin_memory()
+    out_host = torch.empty((TOKENS, HIDDEN), dtype=torch.bfloat16).pin_memory()
+    x_dev = torch.empty_like(x)
+    e2e_steps = max(3, min(args.steps, 50))
+    for _ in range(3):
+        x_dev.copy_(x_host, non_blocking=True)
+        out_host.copy_(layer(x_dev), non_blocking=True)
+    barrier()
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(e2e_steps):
+        x_dev.copy_(x_host, non_blocking=True)
+        out_host.copy_(layer(x_dev), non_blocking=True)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1)
+    if world > 1:
+        t = torch.tensor([e2e_ms], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t[0])
+    e2e_value = TOKENS * world * e2e_steps / (e2e_ms / 1e3)
+    _lib.device_status()
+
+    # ---- roofline of the dominant kernel: grouped gate/up GEMM + SiLU-gate
+    pk = peaks()
+    rows = TOKENS * TOP_K
+    flops = 2.0 * rows * (2 * FFN) * HIDDEN
+    n_local_experts = EXPERTS // world
+    bytes_alg = (n_local_experts * 2 * FFN * HIDDEN * 2      # W13 read once
+                 + rows * HIDDEN * 2 + rows * FFN * 2)        # A read, H written
+    t_s = gemm_ms / 1e3
+    t_tensor = flops / (pk["bf16_sustained"] * 1e12)
+    t_hbm = bytes_alg / (pk["hbm"] * 1e9)
+    traffic = profile_traffic()
+    if t_tensor >= t_hbm:
+        roof = {"bound": "tensor", "achieved": flops / t_s / 1e12,
+                "peak": pk["bf16_sustained"], "unit": "TFLOP/s"}
+    else:
+        roof = {"bound": "hbm", "achieved": bytes_alg / t_s / 1e9,
+                "peak": pk["hbm"], "unit": "GB/s"}
+    roof["frac"] = roof["achieved"] / roof["peak"]
+    roof["traffic"] = traffic
+    roof["kernel"] = "grouped gate/up GEMM + fused SiLU-gate (gemm_bf16_kernel<256,4,false,2>)"
+    roof["algorithmic"] = {"flop": flops, "bytes": bytes_alg, "ms": gemm_ms,
+                           "peak_src": pk["src"] + " (sustained bf16)"}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline_leg(x, layer.w_router, layer.w13, layer.w2)
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "bf16", "data": "synthetic (seeded torch.randn, random-init weights)",
+            "config": {"workload": CONFIG_NAME, "tokens_per_rank": TOKENS, "hidden": HIDDEN,
+                       "experts": EXPERTS, "ffn": FFN, "top_k": TOP_K,
+                       "parallelism": f"ep{world}" if world > 1 else "single",
+                       "l2": "inputs larger than L2 (2.2 GB weights per step)"},
+            "e2e": {"value": e2e_value, "unit": UNIT,
+                    "h2d_bytes_per_step": TOKENS * HIDDEN * 2,
+                    "d2h_bytes_per_step": TOKENS * HIDDEN * 2, "steps": e2e_steps},
+            "gpu_launches": layer.LAUNCHES_PER_CALL * args.steps,
+            "roofline": roof,
+            "cpu_baseline": cpu,
+            "clocks": clocks.summary(wall0, wall1),
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def profile_traffic():
+    """DRAM bytes per launch of the dominant kernel from the committed ncu
+    summary (a `traffic_bytes_per_launch:` line), or None."""
+    p = ROOT / "profiles" / "moe_gemm13_T8192.md"
+    if not p.exists():
+        return None
+    for line in p.read_text().splitlines():
+        if line.strip().startswith("traffic_bytes_per_launch:"):
+            try:
+                return float(line.split(":", 1)[1].strip().split()[0])
+            except ValueError:
+                return None
+    return None
+
+
+# --------------------------------------------------------- reference arm ---
+
+def run_reference(args) -> int:
+    """CPU restatement of the layer on the host cores, bounded sample/step."""
+    world, rank, _ = dist_env()
+    if rank != 0:
+        return 0
+    import numpy as np
+    import oracle
+
+    rng = np.random.default_rng(0)
+    x = oracle.normal_bf16(rng, (1024, HIDDEN))
+    wr = oracle.normal_bf16(rng, (EXPERTS, HIDDEN), 0.02)
+    w13 = oracle.normal_bf16(rng, (EXPERTS, 2 * FFN, HIDDEN), 0.02)
+    w2 = oracle.normal_bf16(rng, (EXPERTS, HIDDEN, FFN), 0.02)
+    t = time.perf_counter()
+    oracle.moe_layer(x[:64], wr, w13, w2, TOP_K)
+    per_tok = (time.perf_counter() - t) / 64
+    total_steps = args.steps + args.warmup
+    sample = int(max(8, min(1024, 90.0 / total_steps / max(per_tok, 1e-6))))
+    for _ in range(args.warmup):
+        oracle.moe_layer(x[:sample], wr, w13, w2, TOP_K)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        oracle.moe_layer(x[:sample], wr, w13, w2, TOP_K)
+    dt = time.perf_counter() - t0
+    value = sample * args.steps / dt
+    cores = oracle.num_threads()
+    desc = (f"{sample} of the 8192 tokens per step through the whole layer; "
+            "the reference has no execution path, so this is the oracle's C restatement")
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT,
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": dt * 1e3 / args.steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": CONFIG_NAME, "tokens_per_step_sample": sample},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port",
+                         "sample": desc},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }), flush=True)
+    return 0
+
+
+def main(argv=None) -> int:
+    args = parse_args(argv)
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,163 @@
+/*
+ * kvm_sm100.h -- C ABI of the B200 (sm_100a) execution backend for KVM
+ * kernel/task-dialect graphs.
+ *
+ * The reference toolkit (feifei-111/KVM) lowers kernel ops to task ops in
+ * src/device/device.cpp but has no way to execute them. Each entry point here
+ * executes one task subgraph on the GPU; the comment on each names the kernel
+ * op (src/ir/dialect/kernel/dialect.cpp) and the task ops it produces
+ * (src/ir/dialect/task/dialect.cpp) that the call stands in for.
+ *
+ * Conventions
+ *  - All tensor pointers are device pointers owned by the caller; sizes are
+ *    element counts; matrices are row-major with the stated row stride.
+ *  - bf16 is passed as 16-bit storage (uint16_t / __nv_bfloat16).
+ *  - `stream` is a cudaStream_t (NULL = the legacy default stream).
+ *  - Every call returns a kvm_status. On failure kvm_sm100_last_error() gives
+ *    a message for the calling thread. Kernels never hang: device-side waits
+ *    are bounded and report KVM_ERR_TIMEOUT through kvm_sm100_device_status().
+ *  - Calls are asynchronous with respect to the host, like a CUDA launch.
+ */
+#ifndef KVM_SM100_H_
+#define KVM_SM100_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define KVM_SM100_ABI_VERSION 1
+
+typedef void* kvm_stream_t; /* cudaStream_t */
+
+enum kvm_status {
+  KVM_OK = 0,
+  KVM_ERR_INVALID_ARG = 1, /* shape, alignment or pointer rejected */
+  KVM_ERR_UNSUPPORTED = 2, /* valid request this build cannot run */
+  KVM_ERR_CUDA = 3,        /* a CUDA runtime/driver call failed */
+  KVM_ERR_TIMEOUT = 4,     /* a bounded device-side wait expired */
+  KVM_ERR_NCCL = 5         /* a collective failed or timed out */
+};
+
+/* Layout of the B operand of a GEMM. */
+enum kvm_b_layout {
+  KVM_B_NK = 0, /* B stored [N, K] (K contiguous): the "weights" layout */
+  KVM_B_KN = 1  /* B stored [K, N] (N contiguous): kernel.matmul's layout */
+};
+
+enum kvm_dtype { KVM_BF16 = 0, KVM_F32 = 1 };
+
+/* ------------------------------------------------------------ runtime --- */
+
+int kvm_sm100_version(void);
+const char* kvm_sm100_last_error(void);
+
+/* Synchronise the current device and read its device-side status word
+ * (bit 0: a bounded wait expired; bit 1: a kernel rejected an index).
+ * Returns KVM_ERR_TIMEOUT / KVM_ERR_INVALID_ARG when a bit is set. */
+int kvm_sm100_device_status(int* status_out, int clear);
+
+/* --------------------------------------------------------------- GEMM --- */
+
+/* D[M,N] = A[M,K] . B  (+ C[M,N] when C != NULL), fp32 accumulation in TMEM.
+ * A: bf16 [M, K], row stride lda; B: bf16 per b_layout with row stride ldb;
+ * C (optional) and D: out_dtype, row stride ldd.
+ * Replaces: kernel.matmul (src/ir/dialect/kernel/dialect.cpp:34) and
+ * kernel.gemm (dialect.cpp:35), whose lowering in src/device/device.cpp:85-106
+ * emits task.tma.gmem_to_smem x2, task.lsu.gmem_to_reg, task.tc.mma_acc and
+ * task.lsu.reg_to_gmem (src/ir/dialect/task/dialect.cpp:33-34,56-61). */
+int kvm_sm100_gemm_bf16(const void* A, int64_t lda, const void* B,
+                        int64_t ldb, int b_layout, const void* C, void* D,
+                        int64_t ldd, int out_dtype, int M, int N, int K,
+                        kvm_stream_t stream);
+
+/* H[M, F] = bf16( SiLU(A.Wg^T) * (A.Wu^T) ), the gated-FFN front half with
+ * the activation fused into the GEMM epilogue. W13 is the packed weight from
+ * kvm_sm100_pack_gate_up ([2F, K], gate/up interleaved in 128-row blocks).
+ * Replaces the composite kernel.matmul x2 -> neg/exp/add/div/mul chain. */
+int kvm_sm100_gemm_bf16_silu_gate(const void* A, int64_t lda, const void* W13,
+                                  void* H, int64_t ldh, int M, int F, int K,
+                                  kvm_stream_t stream);
+
+/* Pack G groups of gate/up weights into the interleaved layout consumed by
+ * the *_silu_gate GEMMs: out[g] = [Wg[g][0:128]; Wu[g][0:128]; Wg[g][128:256];
+ * ...], each block 128 rows of K. w_layout says how Wg/Wu are stored:
+ * KVM_B_NK = [G, F, K], KVM_B_KN = [G, K, F] (transposed while packing).
+ * F must be a multiple of 128. */
+int kvm_sm100_pack_gate_up(const void* Wg, const void* Wu, void* out, int G,
+                           int F, int K, int w_layout, kvm_stream_t stream);
+
+/* Transpose G row-major [R, C] bf16 matrices into [C, R] (weights given in
+ * kernel.matmul's [K, N] layout are converted once to [N, K]). */
+int kvm_sm100_transpose_bf16(const void* in, void* out, int G, int R, int C,
+                             kvm_stream_t stream);
+
+/* ---------------------------------------------------------------- MoE --- */
+
+/* Router GEMM fused with softmax and top-k. logits[T,E] = x[T,H] . Wr^T
+ * (Wr stored [E, H]); probabilities p = softmax(logits) in fp32; topk_idx
+ * [T,k] are the k largest logits per token (ties: lower expert index first,
+ * descending order), topk_w [T,k] their probabilities (no renormalisation).
+ * E must be 64 in this build; 1 <= k <= 8.
+ * Replaces the routing half of kernel.comm.moe_dispatch
+ * (src/ir/dialect/kernel/dialect.cpp:65, passed through to
+ * task.comm.moe_dispatch by src/device/device.cpp:143-147). */
+int kvm_sm100_moe_router_topk(const void* x, const void* Wr, float* logits,
+                              int32_t* topk_idx, float* topk_w, int T, int H,
+                              int E, int k, kvm_stream_t stream);
+
+/* Deterministic expert-major permutation of the T*k (token, slot) pairs:
+ * entries are ordered by (expert, token, slot). Writes expert_offsets [E+1]
+ * (exclusive prefix of per-expert counts), pos [T*k] (row of pair (t,j) in the
+ * permuted order) and src_token [T*k] (token of each permuted row).
+ * workspace: kvm_sm100_moe_permute_workspace(T, k, E) bytes of device memory.
+ * Bit-exact: no atomics decide any position. */
+int64_t kvm_sm100_moe_permute_workspace(int T, int k, int E);
+int kvm_sm100_moe_permute(const int32_t* topk_idx, int T, int k, int E,
+                          int32_t* expert_offsets, int32_t* pos,
+                          int32_t* src_token, void* workspace,
+                          kvm_stream_t stream);
+
+/* xp[pos[t*k+j], :] = x[t, :] for every pair: the token scatter of
+ * moe_dispatch. x: bf16 [T, H]; xp: bf16 [T*k, H]. */
+int kvm_sm100_moe_scatter_rows(const void* x, const int32_t* pos, void* xp,
+                               int T, int k, int H, kvm_stream_t stream);
+
+/* Grouped expert GEMM over the permuted rows. Group g owns rows
+ * [offsets[g], offsets[g+1]) of A and D (offsets live in device memory, as
+ * written by kvm_sm100_moe_permute). B holds G weight matrices [N, K]
+ * (K contiguous), one per group.
+ *   epilogue 0: D[r, 0:N] = bf16(A[r] . B[g]^T)
+ *   epilogue 2: B = packed gate/up ([G, 2F, K]); D[r, 0:F] =
+ *               bf16(SiLU(gate) * up), N passed as 2F.
+ * Replaces kernel.gemm on 3-D expert weights (kernel/dialect.cpp:35). */
+int kvm_sm100_grouped_gemm_bf16(const void* A, const void* B, void* D,
+                                const int32_t* offsets, int G, int rows,
+                                int N, int K, int epilogue,
+                                kvm_stream_t stream);
+
+/* out[t, :] = bf16( sum_{j<k} w[t,j] * Y[pos[t*k+j], :] ), j in order, fp32.
+ * Replaces kernel.comm.moe_combine (src/ir/dialect/kernel/dialect.cpp:66). */
+int kvm_sm100_moe_combine(const void* Y, const int32_t* pos, const float* w,
+                          void* out, int T, int k, int H,
+                          kvm_stream_t stream);
+
+/* ------------------------------------------------------- elementwise --- */
+
+/* y[r, :] = bf16( x[r, :] * rsqrt(mean(x[r, :]^2) + eps) * gamma ), fp32
+ * internally. gamma may be NULL (= 1). Replaces the composite
+ * mul -> matmul(ones/H) -> add(eps) -> rsqrt -> mul (kernel/dialect.cpp:43-46). */
+int kvm_sm100_rmsnorm_bf16(const void* x, const void* gamma, void* y,
+                           int rows, int H, float eps, kvm_stream_t stream);
+
+/* h = bf16( g * sigmoid(g) * u ) elementwise over n bf16 values. Replaces the
+ * composite neg/exp/add/div/mul SiLU-gate chain (kernel/dialect.cpp:43-46). */
+int kvm_sm100_silu_mul_bf16(const void* g, const void* u, void* h, int64_t n,
+                            kvm_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* KVM_SM100_H_ */

@@ -1,0 +1,108 @@
+"""ctypes binding of libkvm_sm100.so, the C ABI declared in include/kvm_sm100.h.
+
+The library is loaded from the package directory only. There is no fallback:
+if the shared object is missing or fails to load, every op raises.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import re
+from pathlib import Path
+
+PKG = Path(__file__).resolve().parent
+LIB_PATH = PKG / "libkvm_sm100.so"
+HEADER = PKG.parent / "include" / "kvm_sm100.h"
+
+KVM_OK = 0
+KVM_ERR_INVALID_ARG = 1
+KVM_ERR_UNSUPPORTED = 2
+KVM_ERR_CUDA = 3
+KVM_ERR_TIMEOUT = 4
+KVM_ERR_NCCL = 5
+
+KVM_B_NK = 0
+KVM_B_KN = 1
+KVM_BF16 = 0
+KVM_F32 = 1
+
+_STATUS_NAMES = {
+    KVM_ERR_INVALID_ARG: "invalid argument",
+    KVM_ERR_UNSUPPORTED: "unsupported",
+    KVM_ERR_CUDA: "CUDA error",
+    KVM_ERR_TIMEOUT: "device wait timed out",
+    KVM_ERR_NCCL: "collective failed",
+}
+
+
+class KvmError(RuntimeError):
+    """A kvm_sm100_* call returned a non-zero kvm_status."""
+
+    def __init__(self, fn: str, code: int, msg: str):
+        super().__init__(f"{fn}: {_STATUS_NAMES.get(code, code)}: {msg}")
+        self.code = code
+
+
+_P = C.c_void_p
+_I = C.c_int
+_I64 = C.c_int64
+_F = C.c_float
+
+# name -> (restype, argtypes); must match include/kvm_sm100.h.
+SIGNATURES = {
+    "kvm_sm100_version": (_I, []),
+    "kvm_sm100_last_error": (C.c_char_p, []),
+    "kvm_sm100_device_status": (_I, [C.POINTER(_I), _I]),
+    "kvm_sm100_gemm_bf16": (_I, [_P, _I64, _P, _I64, _I, _P, _P, _I64, _I, _I, _I, _I, _P]),
+    "kvm_sm100_gemm_bf16_silu_gate": (_I, [_P, _I64, _P, _P, _I64, _I, _I, _I, _P]),
+    "kvm_sm100_pack_gate_up": (_I, [_P, _P, _P, _I, _I, _I, _I, _P]),
+    "kvm_sm100_transpose_bf16": (_I, [_P, _P, _I, _I, _I, _P]),
+    "kvm_sm100_moe_router_topk": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _I, _P]),
+    "kvm_sm100_moe_permute_workspace": (_I64, [_I, _I, _I]),
+    "kvm_sm100_moe_permute": (_I, [_P, _I, _I, _I, _P, _P, _P, _P, _P]),
+    "kvm_sm100_moe_scatter_rows": (_I, [_P, _P, _P, _I, _I, _I, _P]),
+    "kvm_sm100_grouped_gemm_bf16": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, _I, _P]),
+    "kvm_sm100_moe_combine": (_I, [_P, _P, _P, _P, _I, _I, _I, _P]),
+    "kvm_sm100_rmsnorm_bf16": (_I, [_P, _P, _P, _I, _I, _F, _P]),
+    "kvm_sm100_silu_mul_bf16": (_I, [_P, _P, _P, _I64, _P]),
+}
+
+_lib: C.CDLL | None = None
+
+
+def header_symbols() -> list[str]:
+    """Every function name declared in include/kvm_sm100.h."""
+    text = HEADER.read_text()
+    return sorted(set(re.findall(r"\b(kvm_sm100_\w+)\s*\(", text)))
+
+
+def lib() -> C.CDLL:
+    """Load (once) and return the C ABI library, with typed signatures."""
+    global _lib
+    if _lib is None:
+        if not LIB_PATH.exists():
+            raise RuntimeError(
+                f"{LIB_PATH} is missing: build it with `python -m kvm_b200.build`"
+                " (there is no CPU fallback)")
+        handle = C.CDLL(str(LIB_PATH))
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(handle, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = handle
+    return _lib
+
+
+def call(name: str, *args) -> None:
+    """Call kvm_sm100_<name>; raise KvmError on a non-zero status."""
+    L = lib()
+    rc = getattr(L, name)(*args)
+    if rc != KVM_OK:
+        msg = L.kvm_sm100_last_error()
+        raise KvmError(name, rc, msg.decode() if msg else "")
+
+
+def device_status(clear: bool = True) -> int:
+    """Synchronise and return the device status word (raises on error bits)."""
+    v = C.c_int(0)
+    call("kvm_sm100_device_status", C.byref(v), int(clear))
+    return v.value

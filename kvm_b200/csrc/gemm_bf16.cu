@@ -1,0 +1,216 @@
+// Host launchers of the bf16 tcgen05 GEMM: dense GEMM (kernel.matmul /
+// kernel.gemm), the fused SiLU-gate GEMM, the grouped expert GEMM and the
+// router GEMM with fused softmax/top-k.
+#include "gemm_bf16.cuh"
+#include "runtime.h"
+
+namespace kvm {
+namespace {
+
+template <int BN, int STAGES, bool B_MN, int EPI>
+int launch(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p,
+           int grid, cudaStream_t st) {
+  auto kern = gemm_bf16_kernel<BN, STAGES, B_MN, EPI>;
+  constexpr size_t smem = gemm_smem_bytes<BN, STAGES>();
+  KVM_CUDA_TRY(cudaFuncSetAttribute(
+      kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
+  kern<<<grid, kGemmThreads, smem, st>>>(ta, tb, p);
+  KVM_CUDA_TRY(cudaGetLastError());
+  return KVM_OK;
+}
+
+int check_ptr(const void* p, const char* what) {
+  if (!p) return fail(KVM_ERR_INVALID_ARG, std::string(what) + " is NULL");
+  if (!aligned16(p))
+    return fail(KVM_ERR_INVALID_ARG,
+                std::string(what) + " must be 16-byte aligned");
+  return KVM_OK;
+}
+
+#define KVM_TRY(expr)             \
+  do {                            \
+    int kvm_rc_ = (expr);         \
+    if (kvm_rc_ != KVM_OK) return kvm_rc_; \
+  } while (0)
+
+int cdiv(long long a, long long b) { return int((a + b - 1) / b); }
+
+}  // namespace
+}  // namespace kvm
+
+using namespace kvm;
+
+extern "C" int kvm_sm100_gemm_bf16(const void* A, int64_t lda, const void* B,
+                                   int64_t ldb, int b_layout, const void* C,
+                                   void* D, int64_t ldd, int out_dtype, int M,
+                                   int N, int K, kvm_stream_t stream) {
+  if (M <= 0 || N <= 0 || K <= 0)
+    return fail(KVM_ERR_INVALID_ARG, "gemm: M, N, K must be positive");
+  if (b_layout != KVM_B_NK && b_layout != KVM_B_KN)
+    return fail(KVM_ERR_INVALID_ARG, "gemm: unknown b_layout");
+  if (out_dtype != KVM_BF16 && out_dtype != KVM_F32)
+    return fail(KVM_ERR_INVALID_ARG, "gemm: out_dtype must be bf16 or f32");
+  KVM_TRY(check_ptr(A, "gemm: A"));
+  KVM_TRY(check_ptr(B, "gemm: B"));
+  KVM_TRY(check_ptr(D, "gemm: D"));
+  if (C) KVM_TRY(check_ptr(C, "gemm: C"));
+  const int es = out_dtype == KVM_F32 ? 4 : 2;
+  if (lda < K || (lda * 2) % 16 != 0)
+    return fail(KVM_ERR_INVALID_ARG, "gemm: lda must be >= K and a multiple of 8");
+  const long long b_inner = b_layout == KVM_B_NK ? K : N;
+  if (ldb < b_inner || (ldb * 2) % 16 != 0)
+    return fail(KVM_ERR_INVALID_ARG,
+                "gemm: ldb must cover B's contiguous extent and be a multiple of 8");
+  if (ldd < N || (ldd * es) % 16 != 0)
+    return fail(KVM_ERR_INVALID_ARG,
+                "gemm: ldd must be >= N with 16-byte aligned rows");
+  const DeviceInfo* dev = device_info();
+  if (!dev) return KVM_ERR_CUDA;
+
+  GemmParams p{};
+  p.M = M; p.N = N; p.K = K;
+  p.num_groups = 1; p.offsets = nullptr; p.b_group_rows = 0;
+  p.D = D; p.ldd = ldd; p.C = C; p.ldc = ldd;
+  p.status = dev->status;
+
+  const int m_tiles = cdiv(M, kGemmBM);
+  const bool wide = (long long)m_tiles * cdiv(N, 256) >= dev->sm_count;
+  const int BN = wide ? 256 : 128;
+  const int tiles = m_tiles * cdiv(N, BN);
+  const int grid = tiles < dev->sm_count ? tiles : dev->sm_count;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+
+  CUtensorMap ta, tb;
+  KVM_TRY(encode_tmap_2d(&ta, A, K, M, lda * 2, kGemmBK, kGemmBM,
+                         CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
+                         CU_TENSOR_MAP_SWIZZLE_128B));
+  if (b_layout == KVM_B_NK) {
+    KVM_TRY(encode_tmap_2d(&tb, B, K, N, ldb * 2, kGemmBK, BN,
+                           CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
+                           CU_TENSOR_MAP_SWIZZLE_128B));
+  } else {
+    if (N % 8 != 0)
+      return fail(KVM_ERR_INVALID_ARG, "gemm: [K,N] B needs N % 8 == 0");
+    KVM_TRY(encode_tmap_2d(&tb, B, N, K, ldb * 2, 64, kGemmBK,
+                           CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
+                           CU_TENSOR_MAP_SWIZZLE_128B));
+  }
+  const bool mn = b_layout == KVM_B_KN;
+  const bool f32 = out_dtype == KVM_F32;
+  if (wide) {
+    if (!mn && !f32) return launch<256, 4, false, kEpiBf16>(ta, tb, p, grid, st);
+    if (!mn && f32) return launch<256, 4, false, kEpiF32>(ta, tb, p, grid, st);
+    if (mn && !f32) return launch<256, 4, true, kEpiBf16>(ta, tb, p, grid, st);
+    return launch<256, 4, true, kEpiF32>(ta, tb, p, grid, st);
+  }
+  if (!mn && !f32) return launch<128, 6, false, kEpiBf16>(ta, tb, p, grid, st);
+  if (!mn && f32) return launch<128, 6, false, kEpiF32>(ta, tb, p, grid, st);
+  if (mn && !f32) return launch<128, 6, true, kEpiBf16>(ta, tb, p, grid, st);
+  return launch<128, 6, true, kEpiF32>(ta, tb, p, grid, st);
+}
+
+// Shared body of the dense and grouped SiLU-gate / plain grouped launches.
+static int grouped_impl(const void* A, long long lda, const void* B, void* D,
+                        long long ldd, const int32_t* offsets, int G, int rows,
+                        int N, int K, int epilogue, cudaStream_t st) {
+  if (rows < 0 || N <= 0 || K <= 0 || G <= 0 || G > kMaxGroups)
+    return fail(KVM_ERR_INVALID_ARG,
+                "grouped gemm: need rows >= 0, N, K > 0 and 1 <= G <= 256");
+  if (epilogue != kEpiBf16 && epilogue != kEpiSilu)
+    return fail(KVM_ERR_INVALID_ARG, "grouped gemm: epilogue must be 0 or 2");
+  if (epilogue == kEpiSilu && N % 256 != 0)
+    return fail(KVM_ERR_INVALID_ARG,
+                "SiLU-gate gemm: 2F must be a multiple of 256 (F % 128 == 0)");
+  KVM_TRY(check_ptr(A, "grouped gemm: A"));
+  KVM_TRY(check_ptr(B, "grouped gemm: B"));
+  KVM_TRY(check_ptr(D, "grouped gemm: D"));
+  if ((lda * 2) % 16 != 0 || lda < K)
+    return fail(KVM_ERR_INVALID_ARG, "grouped gemm: K must be a multiple of 8");
+  if (rows == 0) return KVM_OK;
+  const DeviceInfo* dev = device_info();
+  if (!dev) return KVM_ERR_CUDA;
+
+  GemmParams p{};
+  p.M = rows; p.N = N; p.K = K;
+  p.num_groups = G; p.offsets = offsets; p.b_group_rows = N;
+  p.D = D; p.ldd = ldd; p.C = nullptr; p.ldc = 0;
+  p.status = dev->status;
+
+  constexpr int BN = 256;
+  const long long ub = (long long)(cdiv(rows, kGemmBM) + G) * cdiv(N, BN);
+  const int grid = ub < dev->sm_count ? int(ub) : dev->sm_count;
+  CUtensorMap ta, tb;
+  KVM_TRY(encode_tmap_2d(&ta, A, K, rows, lda * 2, kGemmBK, kGemmBM,
+                         CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
+                         CU_TENSOR_MAP_SWIZZLE_128B));
+  KVM_TRY(encode_tmap_2d(&tb, B, K, (uint64_t)N * G, (uint64_t)K * 2, kGemmBK,
+                         BN, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
+                         CU_TENSOR_MAP_SWIZZLE_128B));
+  if (epilogue == kEpiSilu)
+    return launch<BN, 4, false, kEpiSilu>(ta, tb, p, grid, st);
+  return launch<BN, 4, false, kEpiBf16>(ta, tb, p, grid, st);
+}
+
+extern "C" int kvm_sm100_gemm_bf16_silu_gate(const void* A, int64_t lda,
+                                             const void* W13, void* H,
+                                             int64_t ldh, int M, int F, int K,
+                                             kvm_stream_t stream) {
+  if (M <= 0 || F <= 0 || F % 128 != 0)
+    return fail(KVM_ERR_INVALID_ARG,
+                "silu-gate gemm: M > 0 and F a positive multiple of 128");
+  if (ldh < F || (ldh * 2) % 16 != 0 || !aligned16(H))
+    return fail(KVM_ERR_INVALID_ARG, "silu-gate gemm: bad H / ldh");
+  // A dense SiLU-gate GEMM is a grouped one with a single group.
+  return grouped_impl(A, lda, W13, H, ldh, nullptr, 1, M, 2 * F, K, kEpiSilu,
+                      static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int kvm_sm100_grouped_gemm_bf16(const void* A, const void* B,
+                                           void* D, const int32_t* offsets,
+                                           int G, int rows, int N, int K,
+                                           int epilogue,
+                                           kvm_stream_t stream) {
+  if (!offsets)
+    return fail(KVM_ERR_INVALID_ARG, "grouped gemm: offsets is NULL");
+  const long long ldd = epilogue == kEpiSilu ? N / 2 : N;
+  if ((ldd * 2) % 16 != 0)
+    return fail(KVM_ERR_INVALID_ARG,
+                "grouped gemm: output rows must be 16-byte multiples");
+  return grouped_impl(A, K, B, D, ldd, offsets, G, rows, N, K, epilogue,
+                      static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int kvm_sm100_moe_router_topk(const void* x, const void* Wr,
+                                         float* logits, int32_t* topk_idx,
+                                         float* topk_w, int T, int H, int E,
+                                         int k, kvm_stream_t stream) {
+  if (E != 64)
+    return fail(KVM_ERR_UNSUPPORTED, "router: this build supports E == 64");
+  if (T <= 0 || H <= 0 || H % 8 != 0 || k < 1 || k > 8)
+    return fail(KVM_ERR_INVALID_ARG,
+                "router: need T > 0, H % 8 == 0 and 1 <= k <= 8");
+  KVM_TRY(check_ptr(x, "router: x"));
+  KVM_TRY(check_ptr(Wr, "router: Wr"));
+  KVM_TRY(check_ptr(logits, "router: logits"));
+  if (!topk_idx || !topk_w)
+    return fail(KVM_ERR_INVALID_ARG, "router: outputs are NULL");
+  const DeviceInfo* dev = device_info();
+  if (!dev) return KVM_ERR_CUDA;
+  GemmParams p{};
+  p.M = T; p.N = E; p.K = H;
+  p.num_groups = 1; p.offsets = nullptr; p.b_group_rows = 0;
+  p.D = logits; p.ldd = E;
+  p.logits = logits; p.topk_idx = topk_idx; p.topk_w = topk_w; p.top_k = k;
+  p.status = dev->status;
+  const int tiles = cdiv(T, kGemmBM);
+  const int grid = tiles < dev->sm_count ? tiles : dev->sm_count;
+  CUtensorMap ta, tb;
+  KVM_TRY(encode_tmap_2d(&ta, x, H, T, (uint64_t)H * 2, kGemmBK, kGemmBM,
+                         CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
+                         CU_TENSOR_MAP_SWIZZLE_128B));
+  KVM_TRY(encode_tmap_2d(&tb, Wr, H, E, (uint64_t)H * 2, kGemmBK, 64,
+                         CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
+                         CU_TENSOR_MAP_SWIZZLE_128B));
+  return launch<64, 8, false, kEpiRouter>(ta, tb, p, grid,
+                                          static_cast<cudaStream_t>(stream));
+}

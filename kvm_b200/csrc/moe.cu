@@ -1,0 +1,264 @@
+// MoE dispatch / combine data movement:
+//   permute  -- deterministic expert-major order of the (token, slot) pairs
+//   scatter  -- token rows -> permuted rows (the dispatch copy)
+//   combine  -- weighted sum of each token's expert outputs
+//
+// The permutation orders pairs by (expert, token, slot). Counting uses shared
+// atomics (order-independent); every position is computed from prefix sums
+// and warp match masks, so the result is identical run to run and equal to a
+// stable sort of the pairs by expert.
+#include <cuda_bf16.h>
+
+#include "runtime.h"
+
+namespace kvm {
+namespace {
+
+constexpr int kPermChunk = 256;  // pairs per block in the permute kernels
+constexpr int kMaxExperts = 1024;
+
+// Per-chunk expert histogram: counts[chunk][e].
+__global__ void __launch_bounds__(kPermChunk)
+    permute_count_kernel(const int* __restrict__ idx, int n, int E,
+                         int* __restrict__ counts, int* status) {
+  extern __shared__ int hist[];
+  for (int e = threadIdx.x; e < E; e += blockDim.x) hist[e] = 0;
+  __syncthreads();
+  const int i = blockIdx.x * kPermChunk + threadIdx.x;
+  if (i < n) {
+    const int e = idx[i];
+    if (e >= 0 && e < E)
+      atomicAdd(&hist[e], 1);
+    else
+      atomicOr(status, kDevBadInput);
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < E; e += blockDim.x)
+    counts[static_cast<long long>(blockIdx.x) * E + e] = hist[e];
+}
+
+// Exclusive scans: base[chunk][e] = offsets[e] + sum_{c' < chunk} counts[c'][e]
+// and offsets[e] = sum_{e' < e} total[e'].  One block, one thread per expert.
+__global__ void permute_scan_kernel(const int* __restrict__ counts,
+                                    int n_chunks, int E, int* __restrict__ base,
+                                    int* __restrict__ offsets) {
+  extern __shared__ int tot[];
+  const int e = threadIdx.x;
+  int run = 0;
+  if (e < E) {
+    for (int c = 0; c < n_chunks; ++c) {
+      const long long o = static_cast<long long>(c) * E + e;
+      base[o] = run;
+      run += counts[o];
+    }
+    tot[e] = run;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int acc = 0;
+    for (int x = 0; x < E; ++x) {
+      const int t = tot[x];
+      tot[x] = acc;
+      acc += t;
+    }
+    offsets[E] = acc;
+  }
+  __syncthreads();
+  if (e < E) {
+    const int off = tot[e];
+    offsets[e] = off;
+    for (int c = 0; c < n_chunks; ++c) base[static_cast<long long>(c) * E + e] += off;
+  }
+}
+
+// Rank of each pair among the same-expert pairs before it in its chunk, plus
+// the chunk base: pos[i]; src_token[pos[i]] = i / k.
+__global__ void __launch_bounds__(kPermChunk)
+    permute_rank_kernel(const int* __restrict__ idx, int n, int k, int E,
+                        const int* __restrict__ base, int* __restrict__ pos,
+                        int* __restrict__ src_token) {
+  constexpr int kWarps = kPermChunk / 32;
+  extern __shared__ int wcount[];  // [kWarps][E]
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  for (int x = threadIdx.x; x < kWarps * E; x += blockDim.x) wcount[x] = 0;
+  __syncthreads();
+  const int i = blockIdx.x * kPermChunk + threadIdx.x;
+  int e = -1;
+  if (i < n) {
+    e = idx[i];
+    if (e < 0 || e >= E) e = -1;
+  }
+  const unsigned peers = __match_any_sync(0xffffffffu, e);
+  const unsigned lt = (1u << lane) - 1u;
+  const int rank_in_warp = __popc(peers & lt);
+  if (e >= 0 && rank_in_warp == 0) wcount[warp * E + e] = __popc(peers);
+  __syncthreads();
+  if (e >= 0) {
+    int r = rank_in_warp;
+    for (int w = 0; w < warp; ++w) r += wcount[w * E + e];
+    const int p = base[static_cast<long long>(blockIdx.x) * E + e] + r;
+    pos[i] = p;
+    src_token[p] = i / k;
+  } else if (i < n) {
+    pos[i] = -1;
+  }
+}
+
+// One block per token: read its row once, write it to each of its k rows.
+__global__ void __launch_bounds__(256)
+    scatter_rows_kernel(const uint4* __restrict__ x, const int* __restrict__ pos,
+                        uint4* __restrict__ xp, int k, int row_vecs,
+                        long long n_rows_out, int* status) {
+  const int t = blockIdx.x;
+  int dst[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    dst[j] = j < k ? pos[static_cast<long long>(t) * k + j] : -1;
+    if (j < k && (dst[j] < 0 || dst[j] >= n_rows_out)) {
+      if (threadIdx.x == 0) atomicOr(status, kDevBadInput);
+      dst[j] = -1;
+    }
+  }
+  const uint4* src = x + static_cast<long long>(t) * row_vecs;
+  for (int v = threadIdx.x; v < row_vecs; v += blockDim.x) {
+    const uint4 val = __ldg(src + v);
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      if (dst[j] >= 0) xp[static_cast<long long>(dst[j]) * row_vecs + v] = val;
+  }
+}
+
+__device__ __forceinline__ void acc_bf16x8(float (&a)[8], uint4 v, float w) {
+  const uint32_t u[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    a[2 * i] = __fmaf_rn(w, __uint_as_float(u[i] << 16), a[2 * i]);
+    a[2 * i + 1] = __fmaf_rn(w, __uint_as_float(u[i] & 0xFFFF0000u), a[2 * i + 1]);
+  }
+}
+
+__device__ __forceinline__ uint32_t pack2(float a, float b) {
+  __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+// One block per token: out[t] = sum_j w[t,j] * Y[pos[t,j]] in fp32, j in order,
+// each step one fused multiply-add (a = fma(w, y, a)) starting from a = 0.
+__global__ void __launch_bounds__(256)
+    combine_kernel(const uint4* __restrict__ Y, const int* __restrict__ pos,
+                   const float* __restrict__ w, uint4* __restrict__ out, int k,
+                   int row_vecs, long long n_rows_y, int* status) {
+  const int t = blockIdx.x;
+  int src[8];
+  float wt[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    src[j] = j < k ? pos[static_cast<long long>(t) * k + j] : -1;
+    wt[j] = j < k ? w[static_cast<long long>(t) * k + j] : 0.f;
+    if (j < k && (src[j] < 0 || src[j] >= n_rows_y)) {
+      if (threadIdx.x == 0) atomicOr(status, kDevBadInput);
+      src[j] = -1;
+    }
+  }
+  for (int v = threadIdx.x; v < row_vecs; v += blockDim.x) {
+    float a[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      if (src[j] >= 0)
+        acc_bf16x8(a, __ldg(Y + static_cast<long long>(src[j]) * row_vecs + v),
+                   wt[j]);
+    uint4 o;
+    o.x = pack2(a[0], a[1]);
+    o.y = pack2(a[2], a[3]);
+    o.z = pack2(a[4], a[5]);
+    o.w = pack2(a[6], a[7]);
+    out[static_cast<long long>(t) * row_vecs + v] = o;
+  }
+}
+
+int n_chunks_of(int T, int k) {
+  return static_cast<int>((static_cast<long long>(T) * k + kPermChunk - 1) /
+                          kPermChunk);
+}
+
+}  // namespace
+}  // namespace kvm
+
+using namespace kvm;
+
+extern "C" int64_t kvm_sm100_moe_permute_workspace(int T, int k, int E) {
+  if (T <= 0 || k <= 0 || E <= 0) return 0;
+  // counts and bases: n_chunks x E ints each.
+  return 2ll * n_chunks_of(T, k) * E * static_cast<int64_t>(sizeof(int));
+}
+
+extern "C" int kvm_sm100_moe_permute(const int32_t* topk_idx, int T, int k,
+                                     int E, int32_t* expert_offsets,
+                                     int32_t* pos, int32_t* src_token,
+                                     void* workspace, kvm_stream_t stream) {
+  if (T <= 0 || k < 1 || k > 8 || E < 1 || E > kMaxExperts)
+    return fail(KVM_ERR_INVALID_ARG,
+                "moe_permute: need T > 0, 1 <= k <= 8, 1 <= E <= 1024");
+  if (static_cast<long long>(T) * k > (1ll << 30))
+    return fail(KVM_ERR_INVALID_ARG, "moe_permute: T*k too large");
+  if (!topk_idx || !expert_offsets || !pos || !src_token || !workspace)
+    return fail(KVM_ERR_INVALID_ARG, "moe_permute: NULL pointer");
+  const DeviceInfo* dev = device_info();
+  if (!dev) return KVM_ERR_CUDA;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int n = T * k;
+  const int nc = n_chunks_of(T, k);
+  int* counts = static_cast<int*>(workspace);
+  int* base = counts + static_cast<long long>(nc) * E;
+  permute_count_kernel<<<nc, kPermChunk, E * sizeof(int), st>>>(
+      topk_idx, n, E, counts, dev->status);
+  KVM_CUDA_TRY(cudaGetLastError());
+  const int scan_threads = ((E + 31) / 32) * 32;
+  permute_scan_kernel<<<1, scan_threads, E * sizeof(int), st>>>(
+      counts, nc, E, base, expert_offsets);
+  KVM_CUDA_TRY(cudaGetLastError());
+  const size_t rank_smem = (kPermChunk / 32) * E * sizeof(int);
+  if (rank_smem > 48 * 1024)
+    KVM_CUDA_TRY(cudaFuncSetAttribute(
+        permute_rank_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        int(rank_smem)));
+  permute_rank_kernel<<<nc, kPermChunk, rank_smem, st>>>(
+      topk_idx, n, k, E, base, pos, src_token);
+  KVM_CUDA_TRY(cudaGetLastError());
+  return KVM_OK;
+}
+
+extern "C" int kvm_sm100_moe_scatter_rows(const void* x, const int32_t* pos,
+                                          void* xp, int T, int k, int H,
+                                          kvm_stream_t stream) {
+  if (T <= 0 || k < 1 || k > 8 || H <= 0 || H % 8 != 0)
+    return fail(KVM_ERR_INVALID_ARG,
+                "moe_scatter_rows: need T > 0, 1 <= k <= 8, H % 8 == 0");
+  if (!x || !pos || !xp || !aligned16(x) || !aligned16(xp))
+    return fail(KVM_ERR_INVALID_ARG,
+                "moe_scatter_rows: NULL or unaligned pointer");
+  const DeviceInfo* dev = device_info();
+  if (!dev) return KVM_ERR_CUDA;
+  scatter_rows_kernel<<<T, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint4*>(x), pos, static_cast<uint4*>(xp), k, H / 8,
+      static_cast<long long>(T) * k, dev->status);
+  KVM_CUDA_TRY(cudaGetLastError());
+  return KVM_OK;
+}
+
+extern "C" int kvm_sm100_moe_combine(const void* Y, const int32_t* pos,
+                                     const float* w, void* out, int T, int k,
+                                     int H, kvm_stream_t stream) {
+  if (T <= 0 || k < 1 || k > 8 || H <= 0 || H % 8 != 0)
+    return fail(KVM_ERR_INVALID_ARG,
+                "moe_combine: need T > 0, 1 <= k <= 8, H % 8 == 0");
+  if (!Y || !pos || !w || !out || !aligned16(Y) || !aligned16(out))
+    return fail(KVM_ERR_INVALID_ARG, "moe_combine: NULL or unaligned pointer");
+  const DeviceInfo* dev = device_info();
+  if (!dev) return KVM_ERR_CUDA;
+  combine_kernel<<<T, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint4*>(Y), pos, w, static_cast<uint4*>(out), k, H / 8,
+      static_cast<long long>(T) * k, dev->status);
+  KVM_CUDA_TRY(cudaGetLastError());
+  return KVM_OK;
+}

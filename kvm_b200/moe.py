@@ -1,0 +1,118 @@
+"""The MoE layer of a kernel-dialect graph executed on one GPU:
+
+    comm.moe_dispatch(x, g)  ->  route (router GEMM + softmax + top-k),
+                                 permute (expert-major order), scatter rows
+    kernel.gemm on 3-D expert weights
+                             ->  grouped GEMM gate/up with fused SiLU-gate,
+                                 grouped GEMM down
+    comm.moe_combine(y, g)   ->  weighted combine
+
+(reference ops: src/ir/dialect/kernel/dialect.cpp:35,65-66; the pass-through
+lowering of dispatch/combine is src/device/device.cpp:143-147.)
+
+All buffers are allocated once, at construction, for ``max_tokens``; a call
+launches eight kernels on the current stream and allocates nothing, so the
+call can be captured in a CUDA graph.
+"""
+from __future__ import annotations
+
+import torch
+
+from . import ops
+from ._lib import call, lib
+
+
+class MoELayer:
+    """Top-k MoE layer with gated (SiLU) experts: H -> F -> H per expert.
+
+    Weights (bf16, device):
+      w_router [E, H]      one row per expert
+      w13      [E, 2F, H]  gate/up packed by ops.pack_gate_up
+      w2       [E, H, F]   down projection, one [H, F] matrix per expert
+    """
+
+    def __init__(self, w_router: torch.Tensor, w13: torch.Tensor, w2: torch.Tensor,
+                 top_k: int, max_tokens: int):
+        E, H = w_router.shape
+        F = w13.shape[1] // 2
+        if w13.shape != (E, 2 * F, H) or w2.shape != (E, H, F):
+            raise ValueError("expected w13 [E, 2F, H] and w2 [E, H, F]")
+        for t, n in ((w_router, "w_router"), (w13, "w13"), (w2, "w2")):
+            if t.dtype != torch.bfloat16 or not t.is_cuda or not t.is_contiguous():
+                raise ValueError(f"{n} must be a contiguous bf16 CUDA tensor")
+        self.E, self.H, self.F, self.k = E, H, F, top_k
+        self.max_tokens = max_tokens
+        self.w_router, self.w13, self.w2 = w_router, w13, w2
+        dev = w_router.device
+        T, k = max_tokens, top_k
+        self.logits = torch.empty((T, E), dtype=torch.float32, device=dev)
+        self.topk_idx = torch.empty((T, k), dtype=torch.int32, device=dev)
+        self.topk_w = torch.empty((T, k), dtype=torch.float32, device=dev)
+        self.offsets = torch.empty(E + 1, dtype=torch.int32, device=dev)
+        self.pos = torch.empty(T * k, dtype=torch.int32, device=dev)
+        self.src_token = torch.empty(T * k, dtype=torch.int32, device=dev)
+        ws = int(lib().kvm_sm100_moe_permute_workspace(T, k, E))
+        self.workspace = torch.empty(max(ws, 16), dtype=torch.uint8, device=dev)
+        self.xp = torch.empty((T * k, H), dtype=torch.bfloat16, device=dev)
+        self.h = torch.empty((T * k, F), dtype=torch.bfloat16, device=dev)
+        self.y = torch.empty((T * k, H), dtype=torch.bfloat16, device=dev)
+        self.out = torch.empty((T, H), dtype=torch.bfloat16, device=dev)
+
+    @classmethod
+    def from_packed(cls, w_router, w13, w2, *, top_k: int, max_tokens: int) -> "MoELayer":
+        return cls(w_router, w13, w2, top_k, max_tokens)
+
+    @classmethod
+    def from_graph_weights(cls, w_router_hk: torch.Tensor, w1: torch.Tensor,
+                           w3: torch.Tensor, w2: torch.Tensor, *, top_k: int,
+                           max_tokens: int) -> "MoELayer":
+        """Weights in the graph's kernel.matmul layout: router [H, E],
+        w1/w3 [E, H, F] (gate/up), w2 [E, F, H]; re-laid out once on the GPU."""
+        wr = ops.transpose(w_router_hk)
+        w13 = ops.pack_gate_up(w1, w3, layout="kn")
+        w2t = ops.transpose(w2)
+        return cls(wr, w13, w2t, top_k, max_tokens)
+
+    @property
+    def last_routing(self) -> ops.Routing:
+        n = self._n
+        return ops.Routing(self.logits[:n], self.topk_idx[:n], self.topk_w[:n])
+
+    @property
+    def last_dispatch(self) -> ops.Dispatch:
+        n = self._n * self.k
+        return ops.Dispatch(self.offsets, self.pos[:n], self.src_token[:n])
+
+    def __call__(self, x: torch.Tensor, probe=None) -> torch.Tensor:
+        """Run the layer on x [T, H]; `probe` = (start, end) CUDA events to
+        record around the gate/up grouped GEMM (for per-kernel timing)."""
+        T, H = x.shape
+        if H != self.H or T > self.max_tokens or T <= 0:
+            raise ValueError(f"x must be [T<= {self.max_tokens}, {self.H}]")
+        if x.dtype != torch.bfloat16 or not x.is_cuda or not x.is_contiguous():
+            raise ValueError("x must be a contiguous bf16 CUDA tensor")
+        self._n = T
+        st = torch.cuda.current_stream().cuda_stream
+        E, F, k = self.E, self.F, self.k
+        call("kvm_sm100_moe_router_topk", x.data_ptr(), self.w_router.data_ptr(),
+             self.logits.data_ptr(), self.topk_idx.data_ptr(), self.topk_w.data_ptr(),
+             T, H, E, k, st)
+        call("kvm_sm100_moe_permute", self.topk_idx.data_ptr(), T, k, E,
+             self.offsets.data_ptr(), self.pos.data_ptr(), self.src_token.data_ptr(),
+             self.workspace.data_ptr(), st)
+        call("kvm_sm100_moe_scatter_rows", x.data_ptr(), self.pos.data_ptr(),
+             self.xp.data_ptr(), T, k, H, st)
+        if probe is not None:
+            probe[0].record()
+        call("kvm_sm100_grouped_gemm_bf16", self.xp.data_ptr(), self.w13.data_ptr(),
+             self.h.data_ptr(), self.offsets.data_ptr(), E, T * k, 2 * F, H, 2, st)
+        if probe is not None:
+            probe[1].record()
+        call("kvm_sm100_grouped_gemm_bf16", self.h.data_ptr(), self.w2.data_ptr(),
+             self.y.data_ptr(), self.offsets.data_ptr(), E, T * k, H, F, 0, st)
+        call("kvm_sm100_moe_combine", self.y.data_ptr(), self.pos.data_ptr(),
+             self.topk_w.data_ptr(), self.out.data_ptr(), T, k, H, st)
+        return self.out[:T]
+
+    # Kernels one call launches (router 1, permute 3, scatter 1, GEMMs 2, combine 1).
+    LAUNCHES_PER_CALL = 8

@@ -1,0 +1,211 @@
+"""CPU oracle for the KVM execution backend -- TEST INFRASTRUCTURE ONLY.
+
+numpy front end over oracle/_build/liboracle.so (oracle/oracle.c, built by
+``make -C oracle``). Only tests/, ``__graft_entry__.smoke()`` and bench.py's
+CPU-baseline leg use this module, as the checker. Parity is UNPINNED: the
+reference has no numeric execution path or golden vectors; the C file states
+which reference op definitions each function restates.
+
+bf16 arrays are carried as numpy uint16 (raw bit patterns).
+"""
+from __future__ import annotations
+
+import ctypes as C
+import subprocess
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+LIB_PATH = HERE / "_build" / "liboracle.so"
+
+_lib: C.CDLL | None = None
+
+
+def build() -> Path:
+    """Compile oracle.c (gcc, OpenMP) into _build/liboracle.so."""
+    r = subprocess.run(["make", "-s", "-C", str(HERE)], capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError(f"oracle build failed:\n{r.stdout}\n{r.stderr}")
+    return LIB_PATH
+
+
+def lib() -> C.CDLL:
+    global _lib
+    if _lib is None:
+        if not LIB_PATH.exists():
+            build()
+        L = C.CDLL(str(LIB_PATH))
+        P, I, I64, F = C.c_void_p, C.c_int, C.c_int64, C.c_float
+        L.orc_f32_to_bf16.restype = C.c_uint16
+        L.orc_f32_to_bf16.argtypes = [F]
+        L.orc_bf16_to_f32.restype = F
+        L.orc_bf16_to_f32.argtypes = [C.c_uint16]
+        L.orc_f32_to_bf16_array.argtypes = [P, P, I64]
+        L.orc_gemm_bf16.argtypes = [P, I64, P, I64, I, P, P, I64, I, I, I, I]
+        L.orc_gemm_silu_gate.argtypes = [P, P, P, P, I, I, I]
+        L.orc_pack_gate_up.argtypes = [P, P, P, I, I, I]
+        L.orc_rmsnorm_bf16.argtypes = [P, P, P, I, I, F]
+        L.orc_silu_mul_bf16.argtypes = [P, P, P, I64]
+        L.orc_moe_topk.argtypes = [P, I, I, I, P, P]
+        L.orc_moe_permute.restype = I
+        L.orc_moe_permute.argtypes = [P, I, I, I, P, P, P]
+        L.orc_moe_scatter_rows.argtypes = [P, P, P, I, I, I]
+        L.orc_grouped_gemm_bf16.argtypes = [P, P, P, P, I, I, I, I]
+        L.orc_moe_combine.argtypes = [P, P, P, P, I, I, I]
+        L.orc_moe_layer.argtypes = [P, P, P, P, P, I, I, I, I, I, P, P, P]
+        L.orc_num_threads.restype = I
+        _lib = L
+    return _lib
+
+
+def _p(a: np.ndarray | None):
+    return None if a is None else a.ctypes.data
+
+
+def _c(a: np.ndarray, dtype) -> np.ndarray:
+    a = np.ascontiguousarray(a)
+    if a.dtype != dtype:
+        raise TypeError(f"expected {dtype}, got {a.dtype}")
+    return a
+
+
+# ------------------------------------------------------------- numerics ---
+
+def f32_to_bf16(x: np.ndarray) -> np.ndarray:
+    """Round fp32 to bf16 (RNE); returns uint16 bit patterns."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    out = np.empty(x.shape, dtype=np.uint16)
+    lib().orc_f32_to_bf16_array(_p(x), _p(out), x.size)
+    return out
+
+
+def bf16_to_f32(h: np.ndarray) -> np.ndarray:
+    h = np.ascontiguousarray(h, dtype=np.uint16)
+    return (h.astype(np.uint32) << 16).view(np.float32)
+
+
+def normal_bf16(rng: np.random.Generator, shape, std: float = 1.0) -> np.ndarray:
+    """Seeded N(0, std^2) values rounded to bf16 (uint16 bits)."""
+    return f32_to_bf16(rng.standard_normal(shape, dtype=np.float32) * np.float32(std))
+
+
+# ------------------------------------------------------------------ ops ---
+
+def gemm(a: np.ndarray, b: np.ndarray, *, b_layout: str = "kn",
+         c: np.ndarray | None = None, out_f32: bool = False) -> np.ndarray:
+    a = _c(a, np.uint16)
+    b = _c(b, np.uint16)
+    M, K = a.shape
+    if b_layout == "kn":
+        N, bkn = b.shape[1], 1
+    else:
+        N, bkn = b.shape[0], 0
+    out = np.empty((M, N), dtype=np.float32 if out_f32 else np.uint16)
+    if c is not None:
+        c = _c(c, out.dtype)
+    lib().orc_gemm_bf16(_p(a), K, _p(b), b.shape[1], bkn, _p(c), _p(out), N,
+                        int(out_f32), M, N, K)
+    return out
+
+
+def gemm_silu_gate(a: np.ndarray, wg: np.ndarray, wu: np.ndarray) -> np.ndarray:
+    a, wg, wu = _c(a, np.uint16), _c(wg, np.uint16), _c(wu, np.uint16)
+    M, K = a.shape
+    F = wg.shape[0]
+    out = np.empty((M, F), dtype=np.uint16)
+    lib().orc_gemm_silu_gate(_p(a), _p(wg), _p(wu), _p(out), M, F, K)
+    return out
+
+
+def pack_gate_up(wg: np.ndarray, wu: np.ndarray) -> np.ndarray:
+    """[G, F, K] gate/up -> [G, 2F, K] interleaved in 128-row blocks."""
+    wg, wu = _c(wg, np.uint16), _c(wu, np.uint16)
+    G, F, K = wg.shape
+    out = np.empty((G, 2 * F, K), dtype=np.uint16)
+    lib().orc_pack_gate_up(_p(wg), _p(wu), _p(out), G, F, K)
+    return out
+
+
+def rmsnorm(x: np.ndarray, gamma: np.ndarray | None, eps: float) -> np.ndarray:
+    x = _c(x, np.uint16)
+    H = x.shape[-1]
+    out = np.empty_like(x)
+    g = None if gamma is None else _c(gamma, np.uint16)
+    lib().orc_rmsnorm_bf16(_p(x), _p(g), _p(out), x.size // H, H, eps)
+    return out
+
+
+def silu_mul(g: np.ndarray, u: np.ndarray) -> np.ndarray:
+    g, u = _c(g, np.uint16), _c(u, np.uint16)
+    out = np.empty_like(g)
+    lib().orc_silu_mul_bf16(_p(g), _p(u), _p(out), g.size)
+    return out
+
+
+def moe_topk(logits: np.ndarray, k: int):
+    logits = _c(logits, np.float32)
+    T, E = logits.shape
+    idx = np.empty((T, k), dtype=np.int32)
+    w = np.empty((T, k), dtype=np.float32)
+    lib().orc_moe_topk(_p(logits), T, E, k, _p(idx), _p(w))
+    return idx, w
+
+
+def moe_permute(idx: np.ndarray, E: int):
+    idx = _c(idx, np.int32)
+    T, k = idx.shape
+    off = np.empty(E + 1, dtype=np.int32)
+    pos = np.empty(T * k, dtype=np.int32)
+    src = np.empty(T * k, dtype=np.int32)
+    rc = lib().orc_moe_permute(_p(idx), T, k, E, _p(off), _p(pos), _p(src))
+    if rc != 0:
+        raise ValueError("expert index out of range")
+    return off, pos, src
+
+
+def moe_scatter_rows(x: np.ndarray, pos: np.ndarray, k: int) -> np.ndarray:
+    x, pos = _c(x, np.uint16), _c(pos, np.int32)
+    T, H = x.shape
+    out = np.zeros((T * k, H), dtype=np.uint16)
+    lib().orc_moe_scatter_rows(_p(x), _p(pos), _p(out), T, k, H)
+    return out
+
+
+def grouped_gemm(a: np.ndarray, w: np.ndarray, offsets: np.ndarray,
+                 silu_gate: bool = False) -> np.ndarray:
+    a, w, offsets = _c(a, np.uint16), _c(w, np.uint16), _c(offsets, np.int32)
+    rows, K = a.shape
+    G, N, _ = w.shape
+    out = np.zeros((rows, N // 2 if silu_gate else N), dtype=np.uint16)
+    lib().orc_grouped_gemm_bf16(_p(a), _p(w), _p(out), _p(offsets), G, N, K, int(silu_gate))
+    return out
+
+
+def moe_combine(y: np.ndarray, pos: np.ndarray, w: np.ndarray) -> np.ndarray:
+    y, pos, w = _c(y, np.uint16), _c(pos, np.int32), _c(w, np.float32)
+    T, k = w.shape
+    H = y.shape[1]
+    out = np.empty((T, H), dtype=np.uint16)
+    lib().orc_moe_combine(_p(y), _p(pos), _p(w), _p(out), T, k, H)
+    return out
+
+
+def moe_layer(x, w_router, w13, w2, k: int):
+    """Whole MoE layer; returns (out, logits, topk_idx, topk_w)."""
+    x, wr = _c(x, np.uint16), _c(w_router, np.uint16)
+    w13, w2 = _c(w13, np.uint16), _c(w2, np.uint16)
+    T, H = x.shape
+    E = wr.shape[0]
+    F = w13.shape[1] // 2
+    out = np.empty((T, H), dtype=np.uint16)
+    logits = np.empty((T, E), dtype=np.float32)
+    idx = np.empty((T, k), dtype=np.int32)
+    tw = np.empty((T, k), dtype=np.float32)
+    lib().orc_moe_layer(_p(x), _p(wr), _p(w13), _p(w2), _p(out), T, H, E, F, k,
+                        _p(logits), _p(idx), _p(tw))
+    return out, logits, idx, tw
+
+
+def num_threads() -> int:
+    return int(lib().orc_num_threads())

@@ -1,0 +1,355 @@
+/*
+ * CPU oracle for the KVM execution backend -- TEST INFRASTRUCTURE ONLY.
+ *
+ * Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline leg load
+ * this library, as the checker; no product code path calls it.
+ *
+ * PARITY UNPINNED. The reference (feifei-111/KVM) has no execution path: it
+ * parses .kvm graphs and lowers kernel ops to task ops
+ * (src/device/device.cpp:129-151) but never computes a value, and ships no
+ * golden vectors or numeric fixtures. This file restates the semantics of the
+ * ops as the reference declares them:
+ *   kernel.matmul  D = A.B            (src/ir/dialect/kernel/dialect.cpp:34)
+ *   kernel.gemm    D = A.B + C        (dialect.cpp:35; task.tc.mma_acc
+ *                                      "D = A.B + C", task/dialect.cpp:34)
+ *   RMSNorm / SiLU-gate as the composites of mul/add/rsqrt and
+ *                  neg/exp/add/div/mul (dialect.cpp:43-46)
+ *   comm.moe_dispatch(x, g) / comm.moe_combine(y, g) (dialect.cpp:65-66),
+ *                  whose routing, permutation and combine are defined by the
+ *                  backend's C ABI (include/kvm_sm100.h).
+ * Arithmetic: inputs bf16, fp32 accumulation (dot products in the fixed
+ * 16-lane order described at gemm_f32), op outputs rounded to bf16 with
+ * round-to-nearest-even.
+ */
+#include <math.h>
+#include <stdint.h>
+#include <stdlib.h>
+#include <string.h>
+
+#ifdef _OPENMP
+#include <omp.h>
+#endif
+
+/* ------------------------------------------------------------ numerics */
+
+static inline float bf2f(uint16_t h) {
+  uint32_t u = (uint32_t)h << 16;
+  float f;
+  memcpy(&f, &u, 4);
+  return f;
+}
+
+/* fp32 -> bf16, round to nearest even; NaN stays a quiet NaN. */
+static inline uint16_t f2bf(float f) {
+  uint32_t u;
+  memcpy(&u, &f, 4);
+  if ((u & 0x7F800000u) == 0x7F800000u && (u & 0x007FFFFFu))
+    return (uint16_t)((u >> 16) | 0x0040u);
+  uint32_t lsb = (u >> 16) & 1u;
+  u += 0x7FFFu + lsb;
+  return (uint16_t)(u >> 16);
+}
+
+uint16_t orc_f32_to_bf16(float f) { return f2bf(f); }
+float orc_bf16_to_f32(uint16_t h) { return bf2f(h); }
+
+void orc_f32_to_bf16_array(const float* in, uint16_t* out, int64_t n) {
+#pragma omp parallel for schedule(static)
+  for (int64_t i = 0; i < n; ++i) out[i] = f2bf(in[i]);
+}
+
+static inline float silu(float g) { return g / (1.0f + expf(-g)); }
+
+/* ---------------------------------------------------------------- GEMM */
+
+/* Summation order of every dot product in this file: 16 partial sums, lane j
+ * accumulating the products with k % 16 == j in ascending k (one rounded
+ * multiply and one rounded add per step, no fused multiply-add), then the
+ * lanes combined pairwise: ((l0+l8)+(l4+l12))+... as written in lanes_sum. */
+#define LANES 16
+
+static inline float lanes_sum(const float* l) {
+  float a[8], b[4], c[2];
+  for (int j = 0; j < 8; ++j) a[j] = l[j] + l[j + 8];
+  for (int j = 0; j < 4; ++j) b[j] = a[j] + a[j + 4];
+  for (int j = 0; j < 2; ++j) c[j] = b[j] + b[j + 2];
+  return c[0] + c[1];
+}
+
+/* dot(a_f32[0:K], bf16 b[0:K]) in the order above. */
+__attribute__((target_clones("avx512f", "avx2", "default"))) static float
+dot_f32_bf16(const float* restrict a, const uint16_t* restrict b, int K) {
+  float l[LANES] = {0};
+  int k = 0;
+  for (; k + LANES <= K; k += LANES)
+    for (int j = 0; j < LANES; ++j) l[j] = l[j] + a[k + j] * bf2f(b[k + j]);
+  for (int j = 0; k + j < K; ++j) l[j] = l[j] + a[k + j] * bf2f(b[k + j]);
+  return lanes_sum(l);
+}
+
+/* acc[i][n] = sum_k A[i][k] * B(k, n) for b_kn = 0 (B stored [N][K]) or
+ * b_kn = 1 (B stored [K][N]; transposed once into [N][K] first). */
+static void gemm_f32(const uint16_t* A, int64_t lda, const uint16_t* B,
+                     int64_t ldb, int b_kn, int M, int N, int K, float* acc) {
+  const uint16_t* Bn = B;
+  int64_t ldbn = ldb;
+  uint16_t* Bt = NULL;
+  if (b_kn) {
+    Bt = (uint16_t*)malloc(sizeof(uint16_t) * (size_t)N * (size_t)K);
+#pragma omp parallel for schedule(static)
+    for (int n = 0; n < N; ++n)
+      for (int k = 0; k < K; ++k) Bt[(int64_t)n * K + k] = B[(int64_t)k * ldb + n];
+    Bn = Bt;
+    ldbn = K;
+  }
+  /* Work items are (row, block of 64 columns) so small-M calls still use
+   * every thread; each item converts its A row once. */
+  const int nb = (N + 63) / 64;
+#pragma omp parallel
+  {
+    float* arow = (float*)malloc(sizeof(float) * (size_t)(K > 0 ? K : 1));
+    int cur = -1;
+#pragma omp for schedule(dynamic, 1)
+    for (int64_t w = 0; w < (int64_t)M * nb; ++w) {
+      const int i = (int)(w / nb), n0 = (int)(w % nb) * 64;
+      if (i != cur) {
+        for (int k = 0; k < K; ++k) arow[k] = bf2f(A[(int64_t)i * lda + k]);
+        cur = i;
+      }
+      const int n1 = n0 + 64 < N ? n0 + 64 : N;
+      for (int n = n0; n < n1; ++n)
+        acc[(int64_t)i * N + n] = dot_f32_bf16(arow, Bn + (int64_t)n * ldbn, K);
+    }
+    free(arow);
+  }
+  free(Bt);
+}
+
+/* kernel.matmul / kernel.gemm: D = A.B (+ C). out_f32 selects fp32 output;
+ * C (optional) has D's dtype and row stride. */
+void orc_gemm_bf16(const uint16_t* A, int64_t lda, const uint16_t* B,
+                   int64_t ldb, int b_kn, const void* C, void* D, int64_t ldd,
+                   int out_f32, int M, int N, int K) {
+  float* acc = (float*)malloc(sizeof(float) * (size_t)M * (size_t)N);
+  gemm_f32(A, lda, B, ldb, b_kn, M, N, K, acc);
+#pragma omp parallel for schedule(static)
+  for (int i = 0; i < M; ++i)
+    for (int n = 0; n < N; ++n) {
+      float v = acc[(int64_t)i * N + n];
+      int64_t o = (int64_t)i * ldd + n;
+      if (out_f32) {
+        if (C) v += ((const float*)C)[o];
+        ((float*)D)[o] = v;
+      } else {
+        if (C) v += bf2f(((const uint16_t*)C)[o]);
+        ((uint16_t*)D)[o] = f2bf(v);
+      }
+    }
+  free(acc);
+}
+
+/* H[M][F] = bf16(SiLU(g) * u), g = A.Wg^T, u = A.Wu^T in fp32 (not rounded
+ * between the GEMM and the activation: the fused epilogue's semantics).
+ * Wg, Wu stored [F][K]. */
+void orc_gemm_silu_gate(const uint16_t* A, const uint16_t* Wg,
+                        const uint16_t* Wu, uint16_t* H, int M, int F, int K) {
+  float* g = (float*)malloc(sizeof(float) * (size_t)M * (size_t)F);
+  float* u = (float*)malloc(sizeof(float) * (size_t)M * (size_t)F);
+  gemm_f32(A, K, Wg, K, 0, M, F, K, g);
+  gemm_f32(A, K, Wu, K, 0, M, F, K, u);
+#pragma omp parallel for schedule(static)
+  for (int64_t i = 0; i < (int64_t)M * F; ++i) H[i] = f2bf(silu(g[i]) * u[i]);
+  free(g);
+  free(u);
+}
+
+/* Gate/up packing: out[g] rows = [Wg[g][0:128]; Wu[g][0:128]; Wg[g][128:256];
+ * ...], inputs [G][F][K]. */
+void orc_pack_gate_up(const uint16_t* Wg, const uint16_t* Wu, uint16_t* out,
+                      int G, int F, int K) {
+  for (int g = 0; g < G; ++g)
+    for (int r = 0; r < 2 * F; ++r) {
+      int blk = r / 256, i = r % 256;
+      int f = blk * 128 + (i % 128);
+      const uint16_t* src = (i < 128 ? Wg : Wu) + ((int64_t)g * F + f) * K;
+      memcpy(out + ((int64_t)g * 2 * F + r) * K, src, sizeof(uint16_t) * K);
+    }
+}
+
+/* ------------------------------------------------------- elementwise */
+
+void orc_rmsnorm_bf16(const uint16_t* x, const uint16_t* gamma, uint16_t* y,
+                      int rows, int H, float eps) {
+#pragma omp parallel for schedule(static)
+  for (int r = 0; r < rows; ++r) {
+    const uint16_t* xr = x + (int64_t)r * H;
+    float ss = 0.0f;
+    for (int i = 0; i < H; ++i) {
+      float v = bf2f(xr[i]);
+      ss += v * v;
+    }
+    float scale = 1.0f / sqrtf(ss / (float)H + eps);
+    for (int i = 0; i < H; ++i) {
+      float v = bf2f(xr[i]) * scale;
+      if (gamma) v *= bf2f(gamma[i]);
+      y[(int64_t)r * H + i] = f2bf(v);
+    }
+  }
+}
+
+void orc_silu_mul_bf16(const uint16_t* g, const uint16_t* u, uint16_t* h,
+                       int64_t n) {
+#pragma omp parallel for schedule(static)
+  for (int64_t i = 0; i < n; ++i) h[i] = f2bf(silu(bf2f(g[i])) * bf2f(u[i]));
+}
+
+/* ------------------------------------------------------------------ MoE */
+
+/* Softmax + top-k over fp32 logits [T][E]. Experts are picked by logit
+ * (softmax is monotone), largest first; among equal logits the lower expert
+ * index wins. Weights are the softmax probabilities (no renormalisation):
+ * p_e = exp(l_e - max) / sum_i exp(l_i - max), sum in index order. */
+void orc_moe_topk(const float* logits, int T, int E, int k, int32_t* idx,
+                  float* w) {
+#pragma omp parallel for schedule(static)
+  for (int t = 0; t < T; ++t) {
+    const float* l = logits + (int64_t)t * E;
+    float mx = l[0];
+    for (int e = 1; e < E; ++e) mx = fmaxf(mx, l[e]);
+    float sum = 0.0f;
+    for (int e = 0; e < E; ++e) sum += expf(l[e] - mx);
+    unsigned char taken[1024];
+    memset(taken, 0, (size_t)E);
+    for (int j = 0; j < k; ++j) {
+      int bi = -1;
+      float best = -INFINITY;
+      for (int e = 0; e < E; ++e)
+        if (!taken[e] && (bi < 0 || l[e] > best)) {
+          best = l[e];
+          bi = e;
+        }
+      taken[bi] = 1;
+      idx[(int64_t)t * k + j] = bi;
+      w[(int64_t)t * k + j] = expf(best - mx) / sum;
+    }
+  }
+}
+
+/* Stable expert-major permutation of the T*k pairs (pair i = t*k + j):
+ * offsets[e] = number of pairs with expert < e; pairs of one expert keep
+ * their i order. pos[i] = permuted row of pair i; src[row] = token. */
+int orc_moe_permute(const int32_t* idx, int T, int k, int E, int32_t* offsets,
+                    int32_t* pos, int32_t* src) {
+  int64_t n = (int64_t)T * k;
+  int32_t* cursor = (int32_t*)calloc((size_t)E + 1, sizeof(int32_t));
+  for (int64_t i = 0; i < n; ++i) {
+    if (idx[i] < 0 || idx[i] >= E) {
+      free(cursor);
+      return -1;
+    }
+    cursor[idx[i] + 1]++;
+  }
+  for (int e = 0; e < E; ++e) cursor[e + 1] += cursor[e];
+  memcpy(offsets, cursor, sizeof(int32_t) * ((size_t)E + 1));
+  for (int64_t i = 0; i < n; ++i) {
+    int32_t p = cursor[idx[i]]++;
+    pos[i] = p;
+    src[p] = (int32_t)(i / k);
+  }
+  free(cursor);
+  return 0;
+}
+
+void orc_moe_scatter_rows(const uint16_t* x, const int32_t* pos, uint16_t* xp,
+                          int T, int k, int H) {
+#pragma omp parallel for schedule(static)
+  for (int t = 0; t < T; ++t)
+    for (int j = 0; j < k; ++j)
+      memcpy(xp + (int64_t)pos[(int64_t)t * k + j] * H, x + (int64_t)t * H,
+             sizeof(uint16_t) * H);
+}
+
+/* Grouped GEMM over permuted rows: for group g, rows [off[g], off[g+1]) of A
+ * times W[g]^T (W stored [G][N][K]). silu_gate = 1: W is packed gate/up
+ * ([G][2F][K], 128-row blocks) and D[r][0:F] = bf16(SiLU(g) * u). */
+void orc_grouped_gemm_bf16(const uint16_t* A, const uint16_t* W, uint16_t* D,
+                           const int32_t* off, int G, int N, int K,
+                           int silu_gate) {
+  for (int g = 0; g < G; ++g) {
+    int r0 = off[g], r1 = off[g + 1];
+    int M = r1 - r0;
+    if (M <= 0) continue;
+    const uint16_t* Wg = W + (int64_t)g * N * K;
+    float* acc = (float*)malloc(sizeof(float) * (size_t)M * (size_t)N);
+    gemm_f32(A + (int64_t)r0 * K, K, Wg, K, 0, M, N, K, acc);
+    if (!silu_gate) {
+      for (int64_t i = 0; i < (int64_t)M * N; ++i)
+        D[(int64_t)r0 * N + i] = f2bf(acc[i]);
+    } else {
+      int F = N / 2;
+#pragma omp parallel for schedule(static)
+      for (int i = 0; i < M; ++i)
+        for (int f = 0; f < F; ++f) {
+          int blk = f / 128, c = f % 128;
+          float gv = acc[(int64_t)i * N + blk * 256 + c];
+          float uv = acc[(int64_t)i * N + blk * 256 + 128 + c];
+          D[((int64_t)r0 + i) * F + f] = f2bf(silu(gv) * uv);
+        }
+    }
+    free(acc);
+  }
+}
+
+/* out[t] = bf16(sum_j w[t][j] * Y[pos[t*k+j]]), fp32, each step a fused
+ * multiply-add in slot order starting from 0. */
+void orc_moe_combine(const uint16_t* Y, const int32_t* pos, const float* w,
+                     uint16_t* out, int T, int k, int H) {
+#pragma omp parallel for schedule(static)
+  for (int t = 0; t < T; ++t)
+    for (int h = 0; h < H; ++h) {
+      float a = 0.0f;
+      for (int j = 0; j < k; ++j)
+        a = fmaf(w[(int64_t)t * k + j],
+                 bf2f(Y[(int64_t)pos[(int64_t)t * k + j] * H + h]), a);
+      out[(int64_t)t * H + h] = f2bf(a);
+    }
+}
+
+/* The whole MoE layer: route -> permute -> scatter -> grouped SiLU-gate GEMM
+ * -> grouped down GEMM -> combine. Weights: Wr [E][H], W13 packed [E][2F][H],
+ * W2 [E][H][F]. Optional outputs (NULL to skip): logits [T][E], idx, topw. */
+void orc_moe_layer(const uint16_t* x, const uint16_t* Wr, const uint16_t* W13,
+                   const uint16_t* W2, uint16_t* out, int T, int H, int E,
+                   int F, int k, float* logits_out, int32_t* idx_out,
+                   float* w_out) {
+  float* logits = (float*)malloc(sizeof(float) * (size_t)T * E);
+  gemm_f32(x, H, Wr, H, 0, T, E, H, logits);
+  int32_t* idx = (int32_t*)malloc(sizeof(int32_t) * (size_t)T * k);
+  float* tw = (float*)malloc(sizeof(float) * (size_t)T * k);
+  orc_moe_topk(logits, T, E, k, idx, tw);
+  int64_t n = (int64_t)T * k;
+  int32_t* off = (int32_t*)malloc(sizeof(int32_t) * ((size_t)E + 1));
+  int32_t* pos = (int32_t*)malloc(sizeof(int32_t) * (size_t)n);
+  int32_t* src = (int32_t*)malloc(sizeof(int32_t) * (size_t)n);
+  orc_moe_permute(idx, T, k, E, off, pos, src);
+  uint16_t* xp = (uint16_t*)malloc(sizeof(uint16_t) * (size_t)n * H);
+  orc_moe_scatter_rows(x, pos, xp, T, k, H);
+  uint16_t* h = (uint16_t*)malloc(sizeof(uint16_t) * (size_t)n * F);
+  orc_grouped_gemm_bf16(xp, W13, h, off, E, 2 * F, H, 1);
+  uint16_t* y = (uint16_t*)malloc(sizeof(uint16_t) * (size_t)n * H);
+  orc_grouped_gemm_bf16(h, W2, y, off, E, H, F, 0);
+  orc_moe_combine(y, pos, tw, out, T, k, H);
+  if (logits_out) memcpy(logits_out, logits, sizeof(float) * (size_t)T * E);
+  if (idx_out) memcpy(idx_out, idx, sizeof(int32_t) * (size_t)n);
+  if (w_out) memcpy(w_out, tw, sizeof(float) * (size_t)n);
+  free(logits); free(idx); free(tw); free(off); free(pos); free(src);
+  free(xp); free(h); free(y);
+}
+
+int orc_num_threads(void) {
+#ifdef _OPENMP
+  return omp_get_max_threads();
+#else
+  return 1;
+#endif
+}

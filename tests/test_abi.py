@@ -1,0 +1,74 @@
+"""The C-ABI library loads, exports every symbol include/kvm_sm100.h declares,
+and rejects bad arguments before touching a GPU (runs on CPU)."""
+import ctypes as C
+import subprocess
+from pathlib import Path
+
+import pytest
+
+from kvm_b200 import _lib
+
+ROOT = Path(__file__).resolve().parent.parent
+
+
+def test_library_exports_every_header_symbol():
+    L = _lib.lib()
+    declared = _lib.header_symbols()
+    assert declared, "no kvm_sm100_* declarations found in the header"
+    missing = [s for s in declared if not hasattr(L, s)]
+    assert not missing, f"declared but not exported: {missing}"
+
+
+def test_python_signatures_cover_header():
+    assert sorted(_lib.SIGNATURES) == _lib.header_symbols()
+
+
+def test_abi_version():
+    assert _lib.lib().kvm_sm100_version() == 1
+
+
+def test_invalid_shapes_rejected_without_gpu():
+    L = _lib.lib()
+    null = None
+    rc = L.kvm_sm100_gemm_bf16(null, 0, null, 0, 0, null, null, 0, 0, 0, 0, 0, null)
+    assert rc == _lib.KVM_ERR_INVALID_ARG
+    assert b"positive" in L.kvm_sm100_last_error()
+    rc = L.kvm_sm100_moe_router_topk(null, null, null, null, null, 16, 64, 32, 2, null)
+    assert rc == _lib.KVM_ERR_UNSUPPORTED
+    rc = L.kvm_sm100_moe_permute(null, 4, 9, 64, null, null, null, null, null)
+    assert rc == _lib.KVM_ERR_INVALID_ARG
+    rc = L.kvm_sm100_rmsnorm_bf16(null, null, null, 4, 12, C.c_float(1e-5), null)
+    assert rc == _lib.KVM_ERR_INVALID_ARG
+    rc = L.kvm_sm100_pack_gate_up(null, null, null, 1, 100, 64, 0, null)
+    assert rc == _lib.KVM_ERR_INVALID_ARG
+
+
+def test_call_raises_kvm_error():
+    with pytest.raises(_lib.KvmError) as ei:
+        _lib.call("kvm_sm100_silu_mul_bf16", None, None, None, 7, None)
+    assert ei.value.code == _lib.KVM_ERR_INVALID_ARG
+
+
+def test_permute_workspace_size():
+    L = _lib.lib()
+    # 8192 tokens x top-2 = 64 chunks of 256 pairs; counts + bases of 64 experts.
+    assert L.kvm_sm100_moe_permute_workspace(8192, 2, 64) == 2 * 64 * 64 * 4
+
+
+def test_product_code_never_imports_the_oracle():
+    offenders = []
+    for p in (ROOT / "kvm_b200").rglob("*"):
+        if p.suffix in (".py", ".cu", ".cuh", ".h", ".cpp") and p.is_file():
+            text = p.read_text(errors="ignore")
+            if "import oracle" in text or "from oracle" in text or "liboracle" in text:
+                offenders.append(str(p))
+    assert not offenders, offenders
+
+
+def test_kernels_built_for_sm100a_only():
+    out = subprocess.run(["cuobjdump", "--list-elf", str(_lib.LIB_PATH)],
+                         capture_output=True, text=True)
+    if out.returncode != 0:
+        pytest.skip("cuobjdump unavailable")
+    archs = {line.split(".")[-2] for line in out.stdout.split() if line.endswith(".cubin")}
+    assert archs == {"sm_100a"}, archs

@@ -1,0 +1,136 @@
+"""MoE dispatch / grouped GEMM / combine parity against the oracle.
+
+Routing indices, permutation, offsets and the scatter copy are compared
+bit-exactly given the same inputs (the GPU's logits are fed to the oracle's
+top-k, since fp32 logits from different accumulation orders can differ in the
+last bits). Combine is bit-exact given the same expert outputs. GEMM outputs
+use the bf16 tolerance: relative L2 error <= 1e-2.
+"""
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from helpers import from_bits, rel_err, to_bits
+from kvm_b200 import ops
+
+pytestmark = pytest.mark.gpu
+
+
+def _weights(rng, E, H, F):
+    wr = oracle.normal_bf16(rng, (E, H), 0.02)
+    w13 = oracle.normal_bf16(rng, (E, 2 * F, H), 0.02)
+    w2 = oracle.normal_bf16(rng, (E, H, F), 0.02)
+    return wr, w13, w2
+
+
+@pytest.mark.parametrize("T,k", [(512, 2), (1, 2), (300, 1), (129, 8)])
+def test_router_topk_bit_exact_given_logits(cuda, T, k):
+    rng = np.random.default_rng(T + k)
+    H, E = 256, 64
+    x = oracle.normal_bf16(rng, (T, H))
+    wr = oracle.normal_bf16(rng, (E, H), 0.02)
+    r = ops.moe_route(from_bits(x, cuda), from_bits(wr, cuda), top_k=k)
+    ops.device_status()
+    logits = r.logits.cpu().numpy()
+    ref_logits = oracle.gemm(x, wr, b_layout="nk", out_f32=True)
+    assert rel_err(logits, ref_logits) < 1e-5
+    idx, w = oracle.moe_topk(logits, k)
+    assert np.array_equal(r.topk_idx.cpu().numpy(), idx)
+    np.testing.assert_allclose(r.topk_w.cpu().numpy(), w, rtol=1e-5, atol=1e-7)
+
+
+def test_router_ties_take_lower_expert(cuda):
+    T, H, E = 128, 64, 64
+    x = np.zeros((T, H), dtype=np.uint16)
+    x[:, 0] = oracle.f32_to_bf16(np.ones(T, dtype=np.float32))
+    wr = np.zeros((E, H), dtype=np.uint16)  # every logit 0 except a few equal maxima
+    wr[[5, 9, 40], 0] = oracle.f32_to_bf16(np.full(3, 2.0, dtype=np.float32))
+    r = ops.moe_route(from_bits(x, cuda), from_bits(wr, cuda), top_k=4)
+    ops.device_status()
+    assert (r.topk_idx.cpu().numpy() == np.array([5, 9, 40, 0])).all()
+
+
+@pytest.mark.parametrize("T,k,E,skew", [(4096, 2, 64, False), (1000, 2, 64, True),
+                                        (7, 3, 64, False), (2048, 8, 16, False),
+                                        (513, 1, 1, False)])
+def test_permute_and_scatter_bit_exact(cuda, T, k, E, skew):
+    rng = np.random.default_rng(T * 3 + k)
+    if skew:   # most pairs on two experts, many experts empty
+        idx = np.where(rng.random((T, k)) < 0.9, rng.integers(0, 2, (T, k)),
+                       rng.integers(0, E, (T, k))).astype(np.int32)
+    else:
+        idx = rng.integers(0, E, (T, k)).astype(np.int32)
+    off, pos, src = oracle.moe_permute(idx, E)
+    d = ops.moe_permute(torch.from_numpy(idx).to(cuda), E)
+    ops.device_status()
+    assert np.array_equal(d.offsets.cpu().numpy(), off)
+    assert np.array_equal(d.pos.cpu().numpy(), pos)
+    assert np.array_equal(d.src_token.cpu().numpy(), src)
+    H = 136
+    x = oracle.normal_bf16(rng, (T, H))
+    xp = ops.moe_scatter_rows(from_bits(x, cuda), d.pos, k)
+    ops.device_status()
+    assert np.array_equal(to_bits(xp), oracle.moe_scatter_rows(x, pos, k))
+
+
+def test_permute_rejects_bad_expert_index(cuda):
+    idx = torch.tensor([[0, 70]], dtype=torch.int32, device=cuda)
+    ops.moe_permute(idx, 64)
+    from kvm_b200._lib import KvmError
+    with pytest.raises(KvmError):
+        ops.device_status()
+
+
+@pytest.mark.parametrize("silu", [False, True])
+def test_grouped_gemm(cuda, silu):
+    rng = np.random.default_rng(21 + silu)
+    G, K = 12, 320
+    N = 512 if silu else 384
+    counts = rng.integers(0, 300, G)
+    counts[3] = 0          # empty group
+    counts[7] = 1          # single row
+    off = np.concatenate([[0], np.cumsum(counts)]).astype(np.int32)
+    rows = int(off[-1])
+    a = oracle.normal_bf16(rng, (rows, K))
+    w = oracle.normal_bf16(rng, (G, N, K), 0.05)
+    ref = oracle.grouped_gemm(a, w, off, silu_gate=silu)
+    got = ops.grouped_matmul(from_bits(a, cuda), from_bits(w, cuda),
+                             torch.from_numpy(off).to(cuda), silu_gate=silu)
+    ops.device_status()
+    g, r = oracle.bf16_to_f32(to_bits(got)), oracle.bf16_to_f32(ref)
+    assert rel_err(g, r) < 1e-2
+
+
+def test_combine_bit_exact(cuda):
+    rng = np.random.default_rng(31)
+    T, k, H, E = 777, 2, 512, 64
+    idx = rng.integers(0, E, (T, k)).astype(np.int32)
+    off, pos, _ = oracle.moe_permute(idx, E)
+    y = oracle.normal_bf16(rng, (T * k, H))
+    w = rng.random((T, k), dtype=np.float32)
+    ref = oracle.moe_combine(y, pos, w)
+    got = ops.moe_combine(from_bits(y, cuda), torch.from_numpy(pos).to(cuda),
+                          torch.from_numpy(w).to(cuda))
+    ops.device_status()
+    assert np.array_equal(to_bits(got), ref)
+
+
+def test_moe_layer_end_to_end(cuda):
+    from kvm_b200.moe import MoELayer
+    rng = np.random.default_rng(41)
+    T, H, E, F, k = 1024, 512, 64, 256, 2
+    x = oracle.normal_bf16(rng, (T, H))
+    wr, w13, w2 = _weights(rng, E, H, F)
+    ref, ref_logits, ref_idx, _ = oracle.moe_layer(x, wr, w13, w2, k)
+    layer = MoELayer.from_packed(from_bits(wr, cuda), from_bits(w13, cuda),
+                                 from_bits(w2, cuda), top_k=k, max_tokens=T)
+    out = layer(from_bits(x, cuda))
+    ops.device_status()
+    gi = layer.last_routing.topk_idx.cpu().numpy()
+    same = (gi == ref_idx).all(axis=1)
+    # Routing can only differ on near-ties of fp32 logits.
+    assert same.mean() > 0.99
+    g = oracle.bf16_to_f32(to_bits(out))[same]
+    r = oracle.bf16_to_f32(ref)[same]
+    assert rel_err(g, r) < 1e-2
