@@ -50,7 +50,21 @@ def parse_args(argv=None):
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true",
                     help="skip the CPU baseline leg (rank 0, N=1)")
-    return ap.parse_args(argv)
+    ap.add_argument("--tokens", type=int, default=TOKENS,
+                    help="tokens per rank (default: the headline 8192; smaller "
+                         "values are profiling cases, not bench lines)")
+    ap.add_argument("--experts", type=int, default=EXPERTS,
+                    help="experts (default 64; profiling cases may use fewer)")
+    args = ap.parse_args(argv)
+    globals()["TOKENS"] = args.tokens
+    globals()["EXPERTS"] = args.experts
+    return args
+
+
+def config_name() -> str:
+    if TOKENS == 8192 and EXPERTS == 64:
+        return CONFIG_NAME
+    return f"profiling_case_T{TOKENS}_H{HIDDEN}_E{EXPERTS}_F{FFN}_top{TOP_K}"
 
 
 def peaks():
@@ -139,8 +153,10 @@ def make_weights(torch, dev, gen):
     return wr, w13, w2
 
 
-def cpu_baseline_leg(x_dev, wr, w13, w2, budget_s: float = 20.0) -> dict:
-    """The oracle (CPU restatement of the layer) on a bounded token sample."""
+def cpu_baseline_leg(x_dev, wr, w13, w2, min_s: float = 10.0) -> dict:
+    """The oracle (CPU restatement of the layer) timed on the host cores: the
+    whole token batch through the layer, repeated until >= min_s of work
+    (at most 3 passes)."""
     import numpy as np
     import torch
     import oracle
@@ -148,18 +164,19 @@ def cpu_baseline_leg(x_dev, wr, w13, w2, budget_s: float = 20.0) -> dict:
     def bits(t):
         return t.contiguous().view(torch.int16).cpu().numpy().view(np.uint16)
 
-    xs, wrs, w13s, w2s = bits(x_dev[:1024]), bits(wr), bits(w13), bits(w2)
+    xs, wrs, w13s, w2s = bits(x_dev), bits(wr), bits(w13), bits(w2)
     oracle.moe_layer(xs[:16], wrs, w13s, w2s, TOP_K)          # warm-up
-    t = time.perf_counter()
-    oracle.moe_layer(xs[:64], wrs, w13s, w2s, TOP_K)
-    per_tok = (time.perf_counter() - t) / 64
-    n = int(max(64, min(1024, budget_s / max(per_tok, 1e-6) / 2)))
-    t = time.perf_counter()
-    oracle.moe_layer(xs[:n], wrs, w13s, w2s, TOP_K)
-    dt = time.perf_counter() - t
+    done, t0 = 0, time.perf_counter()
+    while True:
+        oracle.moe_layer(xs, wrs, w13s, w2s, TOP_K)
+        done += 1
+        dt = time.perf_counter() - t0
+        if dt >= min_s or done >= 3:
+            break
+    n = done * xs.shape[0]
     return {"value": n / dt, "unit": UNIT, "cores": oracle.num_threads(), "kind": "port",
-            "sample": f"first {n} of the 8192 tokens through the whole layer "
-                      f"(same weights), one call, {dt:.2f} s"}
+            "sample": f"all {xs.shape[0]} tokens through the whole layer x{done} "
+                      f"(same inputs and weights), {dt:.1f} s"}
 
 
 def run_ours(args) -> int:
@@ -294,7 +311,7 @@ def run_ours(args) -> int:
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "bf16", "data": "synthetic (seeded torch.randn, random-init weights)",
-            "config": {"workload": CONFIG_NAME, "tokens_per_rank": TOKENS, "hidden": HIDDEN,
+            "config": {"workload": config_name(), "tokens_per_rank": TOKENS, "hidden": HIDDEN,
                        "experts": EXPERTS, "ffn": FFN, "top_k": TOP_K,
                        "parallelism": f"ep{world}" if world > 1 else "single",
                        "l2": "inputs larger than L2 (2.2 GB weights per step)"},
@@ -363,7 +380,7 @@ def run_reference(args) -> int:
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": dt * 1e3 / args.steps, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": CONFIG_NAME, "tokens_per_step_sample": sample},
+        "config": {"workload": config_name(), "tokens_per_step_sample": sample},
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port",
                          "sample": desc},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0,
