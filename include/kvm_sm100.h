@@ -119,6 +119,26 @@ int kvm_sm100_moe_permute(const int32_t* topk_idx, int T, int k, int E,
                           int32_t* src_token, void* workspace,
                           kvm_stream_t stream);
 
+/* Allocation-free variant of kvm_sm100_moe_permute, with the same inputs,
+ * outputs and results. No counterpart in the reference: it exists for callers
+ * that cannot allocate GPU memory while they route tokens -- a host program
+ * that owns every device buffer through its own pool (an FFI host), or a
+ * serving loop that must not call cudaMalloc/cudaFree because they
+ * synchronise the device. The scratch lives in a static device array of
+ * 2 * KVM_SM100_NOALLOC_PERMUTE_MAX_CELLS ints (512 KiB) that every GPU loading
+ * the library holds until exit; sizes with ceil(T*k/256) * E above
+ * KVM_SM100_NOALLOC_PERMUTE_MAX_CELLS are rejected with KVM_ERR_INVALID_ARG.
+ * The first call on a device looks up that array's device address (set-up
+ * done once per device, with that device current); make that first call
+ * before any stream capture. All calls on a device share the array, so calls
+ * whose kernels overlap on the GPU race and must not be issued. Calls no
+ * cudaMalloc, cudaFree or allocating routine. An out-of-range expert index
+ * yields pos = -1 for that pair. */
+#define KVM_SM100_NOALLOC_PERMUTE_MAX_CELLS 65536
+int kvm_sm100_moe_permute_noalloc(const int32_t* topk_idx, int T, int k, int E,
+                                  int32_t* expert_offsets, int32_t* pos,
+                                  int32_t* src_token, kvm_stream_t stream);
+
 /* xp[pos[t*k+j], :] = x[t, :] for every pair: the token scatter of
  * moe_dispatch. x: bf16 [T, H]; xp: bf16 [T*k, H]. */
 int kvm_sm100_moe_scatter_rows(const void* x, const int32_t* pos, void* xp,

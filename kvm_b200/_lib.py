@@ -59,6 +59,7 @@ SIGNATURES = {
     "kvm_sm100_moe_router_topk": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _I, _P]),
     "kvm_sm100_moe_permute_workspace": (_I64, [_I, _I, _I]),
     "kvm_sm100_moe_permute": (_I, [_P, _I, _I, _I, _P, _P, _P, _P, _P]),
+    "kvm_sm100_moe_permute_noalloc": (_I, [_P, _I, _I, _I, _P, _P, _P, _P]),
     "kvm_sm100_moe_scatter_rows": (_I, [_P, _P, _P, _I, _I, _I, _P]),
     "kvm_sm100_grouped_gemm_bf16": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, _I, _P]),
     "kvm_sm100_moe_combine": (_I, [_P, _P, _P, _P, _I, _I, _I, _P]),

@@ -11,6 +11,9 @@
 
 #include "runtime.h"
 
+#include <mutex>
+#include <string>
+
 namespace kvm {
 namespace {
 
@@ -259,6 +262,96 @@ extern "C" int kvm_sm100_moe_combine(const void* Y, const int32_t* pos,
   combine_kernel<<<T, 256, 0, static_cast<cudaStream_t>(stream)>>>(
       static_cast<const uint4*>(Y), pos, w, static_cast<uint4*>(out), k, H / 8,
       static_cast<long long>(T) * k, dev->status);
+  KVM_CUDA_TRY(cudaGetLastError());
+  return KVM_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Allocation-free permute.
+//
+// Some callers cannot allocate GPU memory when they route tokens: a host
+// program that loads this library through its FFI and owns every device
+// buffer through its own memory pool (an allocation outside the pool breaks
+// its accounting and can push the process past its HBM budget), or a serving
+// loop that may not call cudaMalloc/cudaFree because they synchronise the
+// device. For them the permute's scratch (per-chunk expert counts and bases)
+// lives in the fixed array below instead of a caller-provided workspace.
+//
+// Every GPU that loads this library holds the array (512 KiB + 256 B) until
+// the process exits. All calls on a device share it and it keeps the last
+// call's contents: each call overwrites every cell it reads before reading it,
+// so nothing has to start at zero. Calls whose kernels overlap on the GPU
+// (two streams, or two host threads) race on the array and must not be issued.
+namespace kvm {
+namespace {
+
+constexpr int kNoAllocMaxCells = KVM_SM100_NOALLOC_PERMUTE_MAX_CELLS;
+// [0, cells): counts; [cells, 2*cells): bases; then one status word.
+static __device__ __align__(256) int g_permute_scratch[2 * kNoAllocMaxCells + 64];
+
+constexpr int kNoAllocMaxDevices = 64;
+std::mutex g_noalloc_mu;
+int* g_noalloc_ptr[kNoAllocMaxDevices] = {};
+
+// Device address of g_permute_scratch for the current device, looked up once
+// per device (host code may not use the symbol itself: in host code its name
+// is only a host-side stand-in).
+int noalloc_scratch(int** out) {
+  int dev = 0;
+  KVM_CUDA_TRY(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= kNoAllocMaxDevices)
+    return fail(KVM_ERR_UNSUPPORTED, "moe_permute_noalloc: device id too large");
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (!g_noalloc_ptr[dev]) {
+    void* p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_permute_scratch);
+    if (e != cudaSuccess)
+      return fail_cuda(e, "cudaGetSymbolAddress(g_permute_scratch)");
+    g_noalloc_ptr[dev] = static_cast<int*>(p);
+  }
+  *out = g_noalloc_ptr[dev];
+  return KVM_OK;
+}
+
+}  // namespace
+}  // namespace kvm
+
+extern "C" int kvm_sm100_moe_permute_noalloc(const int32_t* topk_idx, int T,
+                                             int k, int E,
+                                             int32_t* expert_offsets,
+                                             int32_t* pos, int32_t* src_token,
+                                             kvm_stream_t stream) {
+  if (T <= 0 || k < 1 || k > 8 || E < 1 || E > kMaxExperts)
+    return fail(KVM_ERR_INVALID_ARG,
+                "moe_permute_noalloc: need T > 0, 1 <= k <= 8, 1 <= E <= 1024");
+  if (static_cast<long long>(T) * k > (1ll << 30))
+    return fail(KVM_ERR_INVALID_ARG, "moe_permute_noalloc: T*k too large");
+  const long long nc = n_chunks_of(T, k);
+  if (nc * E > kNoAllocMaxCells)
+    return fail(KVM_ERR_INVALID_ARG,
+                "moe_permute_noalloc: ceil(T*k/256) * E = " +
+                    std::to_string(nc * E) + " exceeds the static scratch of " +
+                    std::to_string(kNoAllocMaxCells) +
+                    " cells; use kvm_sm100_moe_permute with a workspace");
+  if (!topk_idx || !expert_offsets || !pos || !src_token)
+    return fail(KVM_ERR_INVALID_ARG, "moe_permute_noalloc: NULL pointer");
+  int* scratch = nullptr;
+  if (int rc = noalloc_scratch(&scratch); rc != KVM_OK) return rc;
+  int* counts = scratch;
+  int* base = scratch + kNoAllocMaxCells;
+  int* status = scratch + 2 * kNoAllocMaxCells;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int n = T * k;
+  permute_count_kernel<<<static_cast<int>(nc), kPermChunk, E * sizeof(int), st>>>(
+      topk_idx, n, E, counts, status);
+  KVM_CUDA_TRY(cudaGetLastError());
+  const int scan_threads = ((E + 31) / 32) * 32;
+  permute_scan_kernel<<<1, scan_threads, E * sizeof(int), st>>>(
+      counts, static_cast<int>(nc), E, base, expert_offsets);
+  KVM_CUDA_TRY(cudaGetLastError());
+  const size_t rank_smem = (kPermChunk / 32) * E * sizeof(int);  // <= 32 KiB
+  permute_rank_kernel<<<static_cast<int>(nc), kPermChunk, rank_smem, st>>>(
+      topk_idx, n, k, E, base, pos, src_token);
   KVM_CUDA_TRY(cudaGetLastError());
   return KVM_OK;
 }
