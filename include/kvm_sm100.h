@@ -99,7 +99,7 @@ int kvm_sm100_transpose_bf16(const void* in, void* out, int G, int R, int C,
  * (Wr stored [E, H]); probabilities p = softmax(logits) in fp32; topk_idx
  * [T,k] are the k largest logits per token (ties: lower expert index first,
  * descending order), topk_w [T,k] their probabilities (no renormalisation).
- * E must be 64 in this build; 1 <= k <= 8.
+ * 1 <= E <= 64 in this build; 1 <= k <= min(8, E).
  * Replaces the routing half of kernel.comm.moe_dispatch
  * (src/ir/dialect/kernel/dialect.cpp:65, passed through to
  * task.comm.moe_dispatch by src/device/device.cpp:143-147). */

@@ -184,11 +184,11 @@ extern "C" int kvm_sm100_moe_router_topk(const void* x, const void* Wr,
                                          float* logits, int32_t* topk_idx,
                                          float* topk_w, int T, int H, int E,
                                          int k, kvm_stream_t stream) {
-  if (E != 64)
-    return fail(KVM_ERR_UNSUPPORTED, "router: this build supports E == 64");
-  if (T <= 0 || H <= 0 || H % 8 != 0 || k < 1 || k > 8)
+  if (E < 1 || E > 64)
+    return fail(KVM_ERR_UNSUPPORTED, "router: this build supports 1 <= E <= 64");
+  if (T <= 0 || H <= 0 || H % 8 != 0 || k < 1 || k > 8 || k > E)
     return fail(KVM_ERR_INVALID_ARG,
-                "router: need T > 0, H % 8 == 0 and 1 <= k <= 8");
+                "router: need T > 0, H % 8 == 0 and 1 <= k <= min(8, E)");
   KVM_TRY(check_ptr(x, "router: x"));
   KVM_TRY(check_ptr(Wr, "router: Wr"));
   KVM_TRY(check_ptr(logits, "router: logits"));
@@ -208,7 +208,7 @@ extern "C" int kvm_sm100_moe_router_topk(const void* x, const void* Wr,
   KVM_TRY(encode_tmap_2d(&ta, x, H, T, (uint64_t)H * 2, kGemmBK, kGemmBM,
                          CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
                          CU_TENSOR_MAP_SWIZZLE_128B));
-  KVM_TRY(encode_tmap_2d(&tb, Wr, H, E, (uint64_t)H * 2, kGemmBK, 64,
+  KVM_TRY(encode_tmap_2d(&tb, Wr, H, E, (uint64_t)H * 2, kGemmBK, 64,  // rows >= E read 0
                          CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
                          CU_TENSOR_MAP_SWIZZLE_128B));
   return launch<64, 8, false, kEpiRouter>(ta, tb, p, grid,

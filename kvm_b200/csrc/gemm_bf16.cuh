@@ -24,7 +24,7 @@ enum GemmEpilogue : int {
   kEpiBf16 = 0,    // D = bf16(acc [+ C])
   kEpiF32 = 1,     // D = acc [+ C] (fp32)
   kEpiSilu = 2,    // tile cols [0,BN/2) gate, [BN/2,BN) up -> bf16 SiLU(g)*u
-  kEpiRouter = 3,  // BN = E = 64: logits + softmax + top-k per row
+  kEpiRouter = 3,  // BN = 64 >= E: logits + softmax + top-k per row
 };
 
 constexpr int kGemmBM = 128;
@@ -370,37 +370,45 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             store_row32<false>(dst, nullptr, v, min(32, p.N / 2 - col));
           }
         }
-      } else {  // kEpiRouter: BN == 64 experts
+      } else {  // kEpiRouter: BN == 64 tile columns, the first p.N are experts
         uint32_t r0[32], r1[32];
         tmem_ld32(t_row, r0);
         tmem_ld32(t_row + 32, r1);
         tmem_wait_ld();
         if (row_ok) {
+          const int E = p.N;
           float l[64];
 #pragma unroll
           for (int i = 0; i < 32; ++i) {
             l[i] = __uint_as_float(r0[i]);
             l[32 + i] = __uint_as_float(r1[i]);
           }
-          float4* lrow = reinterpret_cast<float4*>(
-              p.logits + static_cast<long long>(row) * 64);
+          float* lrow = p.logits + static_cast<long long>(row) * E;
+          if (E == 64) {
 #pragma unroll
-          for (int i = 0; i < 16; ++i)
-            lrow[i] = make_float4(l[4 * i], l[4 * i + 1], l[4 * i + 2],
-                                  l[4 * i + 3]);
+            for (int i = 0; i < 16; ++i)
+              reinterpret_cast<float4*>(lrow)[i] =
+                  make_float4(l[4 * i], l[4 * i + 1], l[4 * i + 2], l[4 * i + 3]);
+          } else {
+#pragma unroll
+            for (int i = 0; i < 64; ++i)
+              if (i < E) lrow[i] = l[i];
+          }
           float mx = l[0];
 #pragma unroll
-          for (int i = 1; i < 64; ++i) mx = fmaxf(mx, l[i]);
+          for (int i = 1; i < 64; ++i)
+            if (i < E) mx = fmaxf(mx, l[i]);
           float sum = 0.f;
 #pragma unroll
-          for (int i = 0; i < 64; ++i) sum += expf(l[i] - mx);
+          for (int i = 0; i < 64; ++i)
+            if (i < E) sum += expf(l[i] - mx);
           uint64_t taken = 0;
           for (int j = 0; j < p.top_k; ++j) {
             float best = -INFINITY;
             int bi = -1;
 #pragma unroll
             for (int i = 0; i < 64; ++i) {
-              bool free_i = ((taken >> i) & 1ull) == 0;
+              const bool free_i = i < E && ((taken >> i) & 1ull) == 0;
               if (free_i && (bi < 0 || l[i] > best)) {
                 best = l[i];
                 bi = i;

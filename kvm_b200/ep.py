@@ -1,0 +1,206 @@
+"""Expert-parallel MoE layer: experts sharded over the ranks of a process
+group, token rows exchanged with NCCL point-to-point messages.
+
+This executes `kernel.comm.moe_dispatch` / `kernel.comm.moe_combine` with
+their `ranks` operand (src/ir/dialect/kernel/ops.h:87-88, carried onto the
+task ops by src/device/device.cpp:108-121) when the ranks span several GPUs.
+
+Rank r owns experts [r*E/P, (r+1)*E/P). One forward:
+
+  1. route + permute + scatter the rank's own tokens (local kernels); the
+     permuted rows are expert-major, hence destination-rank-major;
+  2. exchange per-expert row counts (all_to_all of int32 [P, E/P]);
+  3. one device->host copy of the counts and offsets; the host plans one
+     message per (peer, expert) pair with rows, so every rank receives its
+     rows already expert-major (grouped by local expert, then by source rank);
+  4. dispatch: batched isend/irecv of those messages (local pairs are
+     device copies);
+  5. grouped gate/up GEMM with fused SiLU-gate, grouped down GEMM over the
+     local experts;
+  6. combine exchange: the reverse messages return each expert output row to
+     the rank that owns the token, at the row its local permutation gave it;
+  7. weighted combine (local kernel).
+
+Every rank issues the same collectives in the same order; messages between
+a pair are issued in ascending expert order on both sides.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+import torch.distributed as dist
+
+
+@dataclass
+class Plan:
+    """Message plan of one forward (host-side, all sizes in rows)."""
+    send: list      # (peer, src_row, n_rows) from the permuted send buffer
+    recv: list      # (peer, dst_row, n_rows) into the expert-major receive buffer
+    local_offsets: list  # [E/P + 1] row offsets of the local experts
+    recv_rows: int
+
+
+def make_plan(rank: int, world: int, experts: int, send_offsets, recv_counts) -> Plan:
+    """Pure host logic (tested on CPU).
+
+    send_offsets: [E+1] offsets of this rank's permuted rows by global expert.
+    recv_counts:  [P * E/P]; recv_counts[s*Epr + e] = rows rank s sends for
+                  local expert e.
+    Messages to/from one peer are listed in ascending local-expert order.
+    """
+    epr = experts // world
+    send, recv = [], []
+    for d in range(world):
+        for e in range(epr):
+            g = d * epr + e
+            n = int(send_offsets[g + 1] - send_offsets[g])
+            if n:
+                send.append((d, int(send_offsets[g]), n))
+    local = [0]
+    for e in range(epr):
+        local.append(local[-1] + sum(int(recv_counts[s * epr + e]) for s in range(world)))
+    for e in range(epr):
+        row = local[e]
+        for s in range(world):
+            n = int(recv_counts[s * epr + e])
+            if n:
+                recv.append((s, row, n))
+                row += n
+    return Plan(send, recv, local, local[-1])
+
+
+class CudaCompute:
+    """Local compute of one rank on the sm_100a kernels."""
+
+    LAUNCHES = 8  # router 1, permute 3, scatter 1, grouped GEMMs 2, combine 1
+
+    def __init__(self, w_router, w13_local, w2_local, top_k, max_tokens, world):
+        from ._lib import lib
+        self.wr, self.w13, self.w2 = w_router, w13_local, w2_local
+        self.E, self.H = w_router.shape
+        self.F = w13_local.shape[1] // 2
+        self.k = top_k
+        dev = w_router.device
+        T, k, E, H, F = max_tokens, top_k, self.E, self.H, self.F
+        self.logits = torch.empty((T, E), dtype=torch.float32, device=dev)
+        self.idx = torch.empty((T, k), dtype=torch.int32, device=dev)
+        self.topw = torch.empty((T, k), dtype=torch.float32, device=dev)
+        self.offsets = torch.empty(E + 1, dtype=torch.int32, device=dev)
+        self.pos = torch.empty(T * k, dtype=torch.int32, device=dev)
+        self.src = torch.empty(T * k, dtype=torch.int32, device=dev)
+        ws = int(lib().kvm_sm100_moe_permute_workspace(T, k, E))
+        self.ws = torch.empty(max(ws, 16), dtype=torch.uint8, device=dev)
+        self.xp = torch.empty((T * k, H), dtype=torch.bfloat16, device=dev)
+        cap = T * k * world            # every row of every rank on this rank
+        self.recv = torch.empty((cap, H), dtype=torch.bfloat16, device=dev)
+        self.h = torch.empty((cap, F), dtype=torch.bfloat16, device=dev)
+        self.y = torch.empty((cap, H), dtype=torch.bfloat16, device=dev)
+        self.yback = torch.empty((T * k, H), dtype=torch.bfloat16, device=dev)
+        self.out = torch.empty((T, H), dtype=torch.bfloat16, device=dev)
+        self.loc_off = torch.empty(w13_local.shape[0] + 1, dtype=torch.int32, device=dev)
+        self.loc_off_host = torch.empty(w13_local.shape[0] + 1, dtype=torch.int32).pin_memory()
+
+    def dispatch_local(self, x):
+        from ._lib import call
+        T, H = x.shape
+        st = torch.cuda.current_stream().cuda_stream
+        E, k = self.E, self.k
+        call("kvm_sm100_moe_router_topk", x.data_ptr(), self.wr.data_ptr(),
+             self.logits.data_ptr(), self.idx.data_ptr(), self.topw.data_ptr(),
+             T, H, E, k, st)
+        call("kvm_sm100_moe_permute", self.idx.data_ptr(), T, k, E, self.offsets.data_ptr(),
+             self.pos.data_ptr(), self.src.data_ptr(), self.ws.data_ptr(), st)
+        call("kvm_sm100_moe_scatter_rows", x.data_ptr(), self.pos.data_ptr(),
+             self.xp.data_ptr(), T, k, H, st)
+        return self.xp, self.offsets
+
+    def experts(self, rows: int, local_offsets: list):
+        from ._lib import call
+        n = len(local_offsets)
+        self.loc_off_host[:n] = torch.tensor(local_offsets, dtype=torch.int32)
+        self.loc_off[:n].copy_(self.loc_off_host[:n], non_blocking=True)
+        if rows == 0:
+            return self.y
+        st = torch.cuda.current_stream().cuda_stream
+        G, H, F = n - 1, self.H, self.F
+        call("kvm_sm100_grouped_gemm_bf16", self.recv.data_ptr(), self.w13.data_ptr(),
+             self.h.data_ptr(), self.loc_off.data_ptr(), G, rows, 2 * F, H, 2, st)
+        call("kvm_sm100_grouped_gemm_bf16", self.h.data_ptr(), self.w2.data_ptr(),
+             self.y.data_ptr(), self.loc_off.data_ptr(), G, rows, H, F, 0, st)
+        return self.y
+
+    def combine_local(self, T):
+        from ._lib import call
+        st = torch.cuda.current_stream().cuda_stream
+        call("kvm_sm100_moe_combine", self.yback.data_ptr(), self.pos.data_ptr(),
+             self.topw.data_ptr(), self.out.data_ptr(), T, self.k, self.H, st)
+        return self.out[:T]
+
+
+class ExpertParallelMoE:
+    """MoE layer with E/P experts per rank (weak scaling: each rank brings its
+    own tokens). `w13`/`w2` may be the full [E, ...] weights (this rank's slice
+    is taken) or already the local [E/P, ...] slice."""
+
+    def __init__(self, w_router, w13, w2, *, top_k: int, max_tokens: int, rank: int,
+                 world: int, group=None, compute=None):
+        E = w_router.shape[0]
+        if E % world:
+            raise ValueError(f"{E} experts do not split over {world} ranks")
+        self.E, self.world, self.rank, self.k = E, world, rank, top_k
+        self.epr = E // world
+        self.group = group
+        e0 = rank * self.epr
+        if w13.shape[0] == E:
+            w13 = w13[e0:e0 + self.epr].contiguous()
+            w2 = w2[e0:e0 + self.epr].contiguous()
+        self.w_router, self.w13, self.w2 = w_router, w13, w2
+        self.compute = compute or CudaCompute(w_router, w13, w2, top_k, max_tokens, world)
+        self.LAUNCHES_PER_CALL = getattr(self.compute, "LAUNCHES", 0)
+        dev = w_router.device
+        self._send_counts = torch.empty(E, dtype=torch.int32, device=dev)
+        self._recv_counts = torch.empty(E, dtype=torch.int32, device=dev)
+        self.last_plan: Plan | None = None
+
+    def _exchange(self, src_buf, dst_buf, sends, recvs):
+        """Run one batch of messages; rows to/from this rank are local copies."""
+        ops = []
+        local_src = [(s, n) for (p, s, n) in sends if p == self.rank]
+        local_dst = [(d, n) for (p, d, n) in recvs if p == self.rank]
+        for (s, n), (d, n2) in zip(local_src, local_dst):
+            assert n == n2
+            dst_buf[d:d + n].copy_(src_buf[s:s + n])
+        for (p, s, n) in sends:
+            if p != self.rank:
+                ops.append(dist.P2POp(dist.isend, src_buf[s:s + n], self._g(p), self.group))
+        for (p, d, n) in recvs:
+            if p != self.rank:
+                ops.append(dist.P2POp(dist.irecv, dst_buf[d:d + n], self._g(p), self.group))
+        if ops:
+            for w in dist.batch_isend_irecv(ops):
+                w.wait()
+
+    def _g(self, r: int) -> int:
+        return r if self.group is None else dist.get_global_rank(self.group, r)
+
+    def __call__(self, x, probe=None):
+        T = x.shape[0]
+        c = self.compute
+        xp, offsets = c.dispatch_local(x)
+        # per-expert counts of this rank's rows, grouped by destination rank
+        torch.sub(offsets[1:], offsets[:-1], out=self._send_counts)
+        dist.all_to_all_single(self._recv_counts, self._send_counts, group=self.group)
+        both = torch.cat([offsets, self._recv_counts]).cpu()   # the one host sync
+        plan = make_plan(self.rank, self.world, self.E, both[: self.E + 1].tolist(),
+                         both[self.E + 1:].tolist())
+        self.last_plan = plan
+        self._exchange(xp, c.recv, plan.send, plan.recv)
+        if probe is not None:
+            probe[0].record()
+        y = c.experts(plan.recv_rows, plan.local_offsets)
+        if probe is not None:
+            probe[1].record()
+        # reverse: what was received from (peer, row) goes back to (peer, row)
+        self._exchange(y, c.yback, plan.recv, plan.send)
+        return c.combine_local(T)

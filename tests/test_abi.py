@@ -33,7 +33,7 @@ def test_invalid_shapes_rejected_without_gpu():
     rc = L.kvm_sm100_gemm_bf16(null, 0, null, 0, 0, null, null, 0, 0, 0, 0, 0, null)
     assert rc == _lib.KVM_ERR_INVALID_ARG
     assert b"positive" in L.kvm_sm100_last_error()
-    rc = L.kvm_sm100_moe_router_topk(null, null, null, null, null, 16, 64, 32, 2, null)
+    rc = L.kvm_sm100_moe_router_topk(null, null, null, null, null, 16, 64, 96, 2, null)
     assert rc == _lib.KVM_ERR_UNSUPPORTED
     rc = L.kvm_sm100_moe_permute(null, 4, 9, 64, null, null, null, null, null)
     assert rc == _lib.KVM_ERR_INVALID_ARG

@@ -24,10 +24,11 @@ def _weights(rng, E, H, F):
     return wr, w13, w2
 
 
-@pytest.mark.parametrize("T,k", [(512, 2), (1, 2), (300, 1), (129, 8)])
-def test_router_topk_bit_exact_given_logits(cuda, T, k):
+@pytest.mark.parametrize("T,k,E", [(512, 2, 64), (1, 2, 64), (300, 1, 64), (129, 8, 64),
+                                   (700, 2, 16), (64, 3, 5)])
+def test_router_topk_bit_exact_given_logits(cuda, T, k, E):
     rng = np.random.default_rng(T + k)
-    H, E = 256, 64
+    H = 256
     x = oracle.normal_bf16(rng, (T, H))
     wr = oracle.normal_bf16(rng, (E, H), 0.02)
     r = ops.moe_route(from_bits(x, cuda), from_bits(wr, cuda), top_k=k)
