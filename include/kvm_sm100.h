@@ -163,6 +163,38 @@ int kvm_sm100_moe_combine(const void* Y, const int32_t* pos, const float* w,
                           void* out, int T, int k, int H,
                           kvm_stream_t stream);
 
+/* ---------------------------------------------------------------- FP8 --- */
+
+/* FP8 e4m3 W8A8 GEMM with 128x128 fp32 block scales, bf16 output:
+ *   D[m,n] = bf16( sum_kb s * P_kb[m,n] ),  s = sA[m/128][kb] * sW[n/128][kb],
+ *   P_kb = sum over the 128-deep K block kb of Aq[m,k] * Wq[n,k] (fp32),
+ *   accumulated acc = fma(P_kb, s, acc) in ascending kb.
+ * Aq: e4m3 [M, K] (K contiguous); sA: fp32 [ceil(M/128), K/128].
+ * Wq: e4m3 [N, K] (K contiguous; weights in kernel.matmul's [K, N] layout are
+ * converted once with kvm_sm100_transpose_u8 / kvm_sm100_transpose_f32);
+ * sW: fp32 [N/128, K/128]. K % 128 == 0, N % 128 == 0.
+ * The reference cannot express this op (src/ir/dialect/dtype.h:13-20 has no
+ * fp8); it is the sm_100a form of task.tc.mma_acc (task/dialect.cpp:34) on
+ * e4m3 operands. */
+int kvm_sm100_gemm_fp8_blockscaled(const void* Aq, const float* sA,
+                                   const void* Wq, const float* sW, void* D,
+                                   int64_t ldd, int M, int N, int K,
+                                   kvm_stream_t stream);
+
+/* Quantise x [R, C] (x_dtype KVM_BF16 or KVM_F32) to e4m3 per 128x128 block:
+ * scale s = amax(|x| over the block) / 448 (1 for an all-zero block),
+ * q = e4m3(x / s) with IEEE division, round-to-nearest-even, saturating to
+ * +-448. scales: fp32 [ceil(R/128), ceil(C/128)]. */
+int kvm_sm100_quantize_e4m3_block128(const void* x, int x_dtype, void* q,
+                                     float* scales, int R, int C,
+                                     kvm_stream_t stream);
+
+/* Byte / fp32 matrix transposes [R, C] -> [C, R] (one-time weight re-layout). */
+int kvm_sm100_transpose_u8(const void* in, void* out, int R, int C,
+                           kvm_stream_t stream);
+int kvm_sm100_transpose_f32(const float* in, float* out, int R, int C,
+                            kvm_stream_t stream);
+
 /* ------------------------------------------------------- elementwise --- */
 
 /* y[r, :] = bf16( x[r, :] * rsqrt(mean(x[r, :]^2) + eps) * gamma ), fp32

@@ -63,6 +63,10 @@ SIGNATURES = {
     "kvm_sm100_moe_scatter_rows": (_I, [_P, _P, _P, _I, _I, _I, _P]),
     "kvm_sm100_grouped_gemm_bf16": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, _I, _P]),
     "kvm_sm100_moe_combine": (_I, [_P, _P, _P, _P, _I, _I, _I, _P]),
+    "kvm_sm100_gemm_fp8_blockscaled": (_I, [_P, _P, _P, _P, _P, _I64, _I, _I, _I, _P]),
+    "kvm_sm100_quantize_e4m3_block128": (_I, [_P, _I, _P, _P, _I, _I, _P]),
+    "kvm_sm100_transpose_u8": (_I, [_P, _P, _I, _I, _P]),
+    "kvm_sm100_transpose_f32": (_I, [_P, _P, _I, _I, _P]),
     "kvm_sm100_rmsnorm_bf16": (_I, [_P, _P, _P, _I, _I, _F, _P]),
     "kvm_sm100_silu_mul_bf16": (_I, [_P, _P, _P, _I64, _P]),
 }

@@ -143,6 +143,70 @@ def silu_gate_matmul(a: torch.Tensor, w13: torch.Tensor,
     return out
 
 
+# -------------------------------------------------------------------- FP8 ---
+
+def quantize_e4m3(x: torch.Tensor):
+    """128x128 block quantisation: returns (q uint8 [R, C] e4m3 bits, scales fp32
+    [ceil(R/128), ceil(C/128)]); s = amax/448, q = e4m3_rn_satfinite(x / s)."""
+    if x.dtype not in (torch.bfloat16, torch.float32):
+        raise TypeError("x must be bf16 or fp32")
+    _check(x, "x", x.dtype, 2)
+    if not x.is_contiguous():
+        raise ValueError("x must be contiguous")
+    R, Cc = x.shape
+    q = torch.empty((R, Cc), dtype=torch.uint8, device=x.device)
+    s = torch.empty(((R + 127) // 128, (Cc + 127) // 128), dtype=torch.float32,
+                    device=x.device)
+    call("kvm_sm100_quantize_e4m3_block128", x.data_ptr(),
+         KVM_F32 if x.dtype == torch.float32 else KVM_BF16, q.data_ptr(), s.data_ptr(),
+         R, Cc, _stream())
+    return q, s
+
+
+def transpose_u8(x: torch.Tensor) -> torch.Tensor:
+    _check(x, "x", torch.uint8, 2)
+    x = x.contiguous()
+    out = torch.empty((x.shape[1], x.shape[0]), dtype=torch.uint8, device=x.device)
+    call("kvm_sm100_transpose_u8", x.data_ptr(), out.data_ptr(), x.shape[0], x.shape[1],
+         _stream())
+    return out
+
+
+def transpose_f32(x: torch.Tensor) -> torch.Tensor:
+    _check(x, "x", torch.float32, 2)
+    x = x.contiguous()
+    out = torch.empty((x.shape[1], x.shape[0]), dtype=torch.float32, device=x.device)
+    call("kvm_sm100_transpose_f32", x.data_ptr(), out.data_ptr(), x.shape[0], x.shape[1],
+         _stream())
+    return out
+
+
+def matmul_fp8(aq: torch.Tensor, sa: torch.Tensor, wq: torch.Tensor, sw: torch.Tensor,
+               out: torch.Tensor | None = None) -> torch.Tensor:
+    """D = sum_kb sA*sW * (Aq . Wq^T) over 128-deep blocks, bf16 out.
+
+    aq: uint8 e4m3 [M, K]; sa fp32 [ceil(M/128), K/128]; wq: uint8 e4m3 [N, K];
+    sw fp32 [N/128, K/128].
+    """
+    _check(aq, "aq", torch.uint8, 2)
+    _check(wq, "wq", torch.uint8, 2)
+    _check(sa, "sa", torch.float32, 2)
+    _check(sw, "sw", torch.float32, 2)
+    M, K = aq.shape
+    N = wq.shape[0]
+    if wq.shape[1] != K or sa.shape != ((M + 127) // 128, K // 128) or \
+            sw.shape != (N // 128, K // 128):
+        raise ValueError("fp8 operand / scale shapes disagree")
+    for t, n in ((aq, "aq"), (wq, "wq"), (sa, "sa"), (sw, "sw")):
+        if not t.is_contiguous():
+            raise ValueError(f"{n} must be contiguous")
+    if out is None:
+        out = torch.empty((M, N), dtype=torch.bfloat16, device=aq.device)
+    call("kvm_sm100_gemm_fp8_blockscaled", aq.data_ptr(), sa.data_ptr(), wq.data_ptr(),
+         sw.data_ptr(), out.data_ptr(), _rowmajor(out, "out"), M, N, K, _stream())
+    return out
+
+
 # ------------------------------------------------------------ elementwise ---
 
 def rmsnorm(x: torch.Tensor, gamma: torch.Tensor | None = None, eps: float = 1e-5,
@@ -288,7 +352,8 @@ def device_status() -> int:
 
 
 __all__ = [
-    "matmul", "gemm", "pack_gate_up", "transpose", "silu_gate_matmul", "rmsnorm",
+    "matmul", "gemm", "pack_gate_up", "quantize_e4m3", "matmul_fp8", "transpose_u8",
+    "transpose_f32", "transpose", "silu_gate_matmul", "rmsnorm",
     "silu_mul", "moe_route", "moe_permute", "moe_scatter_rows", "grouped_matmul",
     "moe_combine", "Routing", "Dispatch", "device_status", "KVM_B_KN", "KVM_B_NK",
 ]

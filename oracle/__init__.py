@@ -55,6 +55,11 @@ def lib() -> C.CDLL:
         L.orc_moe_combine.argtypes = [P, P, P, P, I, I, I]
         L.orc_moe_layer.argtypes = [P, P, P, P, P, I, I, I, I, I, P, P, P]
         L.orc_num_threads.restype = I
+        L.orc_f32_to_e4m3_array.argtypes = [P, P, I64]
+        L.orc_e4m3_to_f32.restype = F
+        L.orc_e4m3_to_f32.argtypes = [C.c_uint8]
+        L.orc_quantize_e4m3_block128.argtypes = [P, I, I, P, P]
+        L.orc_gemm_fp8_blockscaled.argtypes = [P, P, P, P, P, I, I, I]
         _lib = L
     return _lib
 
@@ -205,6 +210,52 @@ def moe_layer(x, w_router, w13, w2, k: int):
     lib().orc_moe_layer(_p(x), _p(wr), _p(w13), _p(w2), _p(out), T, H, E, F, k,
                         _p(logits), _p(idx), _p(tw))
     return out, logits, idx, tw
+
+
+# ------------------------------------------------------------------ FP8 ---
+
+def f32_to_e4m3(x: np.ndarray) -> np.ndarray:
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    out = np.empty(x.shape, dtype=np.uint8)
+    lib().orc_f32_to_e4m3_array(_p(x), _p(out), x.size)
+    return out
+
+
+def e4m3_to_f32(q: np.ndarray) -> np.ndarray:
+    lut = np.array([lib().orc_e4m3_to_f32(v) for v in range(256)], dtype=np.float32)
+    return lut[np.asarray(q, dtype=np.uint8)]
+
+
+def quantize_e4m3_block128(x: np.ndarray):
+    x = _c(np.asarray(x, dtype=np.float32), np.float32)
+    R, Cc = x.shape
+    q = np.empty((R, Cc), dtype=np.uint8)
+    s = np.empty(((R + 127) // 128, (Cc + 127) // 128), dtype=np.float32)
+    lib().orc_quantize_e4m3_block128(_p(x), R, Cc, _p(q), _p(s))
+    return q, s
+
+
+def gemm_fp8_blockscaled(aq, sa, wq, sw) -> np.ndarray:
+    aq, wq = _c(aq, np.uint8), _c(wq, np.uint8)
+    sa, sw = _c(sa, np.float32), _c(sw, np.float32)
+    M, K = aq.shape
+    N = wq.shape[0]
+    out = np.empty((M, N), dtype=np.uint16)
+    lib().orc_gemm_fp8_blockscaled(_p(aq), _p(sa), _p(wq), _p(sw), _p(out), M, N, K)
+    return out
+
+
+def cuda_host_e4m3(x: np.ndarray) -> np.ndarray:
+    """CUDA's host-side saturating e4m3 conversion (the known answer)."""
+    so = HERE / "_build" / "libfp8pin.so"
+    if not so.exists():
+        build()
+    L = C.CDLL(str(so))
+    L.pin_f32_to_e4m3_array.argtypes = [C.c_void_p, C.c_void_p, C.c_int64]
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    out = np.empty(x.shape, dtype=np.uint8)
+    L.pin_f32_to_e4m3_array(_p(x), _p(out), x.size)
+    return out
 
 
 def num_threads() -> int:

@@ -353,3 +353,100 @@ int orc_num_threads(void) {
   return 1;
 #endif
 }
+
+/* ------------------------------------------------------------------ FP8 */
+
+/* e4m3 ("E4M3FN" in the OCP 8-bit floating point specification): 1 sign bit,
+ * 4 exponent bits with bias 7, 3 mantissa bits; exponent field 0 holds the
+ * subnormals m * 2^-9; no infinities; S.1111.111 is NaN, so the largest finite
+ * magnitude is 1.75 * 2^8 = 448. Conversion from fp32 rounds once to the
+ * nearest representable value (ties to even mantissa) and saturates: every
+ * magnitude >= 448, infinities included, becomes +-448. NaN becomes 0x7F
+ * with the input's sign. */
+uint8_t orc_f32_to_e4m3(float x) {
+  uint32_t u;
+  memcpy(&u, &x, 4);
+  const uint8_t sign = (uint8_t)((u >> 24) & 0x80u);
+  if ((u & 0x7F800000u) == 0x7F800000u && (u & 0x007FFFFFu)) return sign | 0x7Fu;
+  const float a = fabsf(x);
+  if (a >= 448.0f) return sign | 0x7Eu;
+  if (a < 0.015625f) { /* below 2^-6: subnormal quantum 2^-9 */
+    const int m = (int)nearbyintf(a * 512.0f); /* exact scaling, one rounding */
+    return sign | (uint8_t)m;                  /* m == 8 encodes 2^-6 */
+  }
+  int e2;
+  (void)frexpf(a, &e2); /* a = f * 2^e2, f in [0.5, 1) */
+  int E = e2 - 1;       /* a in [2^E, 2^(E+1)) */
+  int m = (int)nearbyintf(ldexpf(a, 3 - E)); /* 8..16 */
+  if (m == 16) {
+    m = 8;
+    E += 1;
+  }
+  return sign | (uint8_t)(((E + 7) << 3) | (m - 8));
+}
+
+float orc_e4m3_to_f32(uint8_t v) {
+  const int s = v >> 7, e = (v >> 3) & 15, m = v & 7;
+  float r;
+  if (e == 15 && m == 7) return s ? -NAN : NAN;
+  if (e == 0)
+    r = ldexpf((float)m, -9);
+  else
+    r = ldexpf(1.0f + (float)m / 8.0f, e - 7);
+  return s ? -r : r;
+}
+
+void orc_f32_to_e4m3_array(const float* in, uint8_t* out, int64_t n) {
+#pragma omp parallel for schedule(static)
+  for (int64_t i = 0; i < n; ++i) out[i] = orc_f32_to_e4m3(in[i]);
+}
+
+/* Block quantisation of x [R][C] (fp32): per 128x128 block s = amax / 448
+ * (1 when amax == 0), q = e4m3(x / s); scales [ceil(R/128)][ceil(C/128)]. */
+void orc_quantize_e4m3_block128(const float* x, int R, int C, uint8_t* q,
+                                float* scales) {
+  const int br = (R + 127) / 128, bc = (C + 127) / 128;
+#pragma omp parallel for collapse(2) schedule(static)
+  for (int i = 0; i < br; ++i)
+    for (int j = 0; j < bc; ++j) {
+      float amax = 0.0f;
+      for (int r = i * 128; r < R && r < i * 128 + 128; ++r)
+        for (int c = j * 128; c < C && c < j * 128 + 128; ++c)
+          amax = fmaxf(amax, fabsf(x[(int64_t)r * C + c]));
+      const float s = amax > 0.0f ? amax / 448.0f : 1.0f;
+      scales[(int64_t)i * bc + j] = s;
+      for (int r = i * 128; r < R && r < i * 128 + 128; ++r)
+        for (int c = j * 128; c < C && c < j * 128 + 128; ++c)
+          q[(int64_t)r * C + c] = orc_f32_to_e4m3(x[(int64_t)r * C + c] / s);
+    }
+}
+
+/* D[m][n] = bf16( acc ), acc = fma(P_kb, sA[m/128][kb] * sW[n/128][kb], acc)
+ * over kb ascending; P_kb = sum_{k in block} Aq[m][k] * Wq[n][k] in fp32 in
+ * the 16-lane order of dot_f32_bf16 (e4m3 products are exact in fp32).
+ * Aq [M][K], Wq [N][K], K % 128 == 0. */
+void orc_gemm_fp8_blockscaled(const uint8_t* Aq, const float* sA,
+                              const uint8_t* Wq, const float* sW, uint16_t* D,
+                              int M, int N, int K) {
+  const int kbs = K / 128;
+  float lut[256];
+  for (int v = 0; v < 256; ++v) lut[v] = orc_e4m3_to_f32((uint8_t)v);
+#pragma omp parallel for schedule(dynamic, 1)
+  for (int m = 0; m < M; ++m) {
+    float a[128];
+    for (int n = 0; n < N; ++n) {
+      float acc = 0.0f;
+      for (int kb = 0; kb < kbs; ++kb) {
+        const uint8_t* ar = Aq + (int64_t)m * K + kb * 128;
+        const uint8_t* wr = Wq + (int64_t)n * K + kb * 128;
+        float l[LANES] = {0};
+        for (int k = 0; k < 128; ++k) a[k] = lut[ar[k]];
+        for (int k = 0; k < 128; k += LANES)
+          for (int j = 0; j < LANES; ++j) l[j] = l[j] + a[k + j] * lut[wr[k + j]];
+        const float s = sA[(int64_t)(m / 128) * kbs + kb] * sW[(int64_t)(n / 128) * kbs + kb];
+        acc = fmaf(lanes_sum(l), s, acc);
+      }
+      D[(int64_t)m * N + n] = f2bf(acc);
+    }
+  }
+}
