@@ -329,6 +329,7 @@ def run_ours(args) -> int:
         }
         print(json.dumps(line), flush=True)
     if world > 1:
+        layer.close()
         barrier()
         dist.destroy_process_group()
     return 0

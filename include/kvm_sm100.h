@@ -163,6 +163,71 @@ int kvm_sm100_moe_combine(const void* Y, const int32_t* pos, const float* w,
                           void* out, int T, int k, int H,
                           kvm_stream_t stream);
 
+/* -------------------------------------------- expert parallel (NVLink) --- */
+
+/* Peer memory for the expert-parallel exchange among the `world` ranks of one
+ * node (one process per GPU). Every rank allocates its own buffers with
+ * kvm_sm100_ipc_alloc and exchanges their IPC handles (64 bytes each, from
+ * kvm_sm100_ipc_get_handle) out of band; each rank then fills its table with
+ * its own pointers at [rank] and opened peer pointers elsewhere.
+ *   recv[r]  bf16 [cap_rows, H]  rows routed to rank r's experts
+ *   y[r]     bf16 [cap_rows, H]  rank r's expert outputs (same rows)
+ *   cnt[r]   int32 [world, E]    per-source, per-expert pair counts
+ *   flags[r] uint32 [3, world]   count / data / outputs-ready epochs
+ * Executes kernel.comm.moe_dispatch / moe_combine across the op's `ranks`
+ * (src/ir/dialect/kernel/ops.h:87-88; the rank list survives lowering,
+ * src/device/device.cpp:108-121) as peer stores and loads over NVLink. */
+#define KVM_EP_MAX_RANKS 8
+typedef struct kvm_ep_peers {
+  int32_t rank, world, E, H, k, pad_;
+  void* recv[KVM_EP_MAX_RANKS];
+  void* y[KVM_EP_MAX_RANKS];
+  void* cnt[KVM_EP_MAX_RANKS];
+  void* flags[KVM_EP_MAX_RANKS];
+} kvm_ep_peers;
+
+int kvm_sm100_ipc_alloc(int64_t bytes, void** ptr); /* cudaMalloc + zero */
+int kvm_sm100_ipc_free(void* ptr);
+int kvm_sm100_ipc_get_handle(const void* ptr, void* handle64);
+int kvm_sm100_ipc_open_handle(const void* handle64, void** peer_ptr);
+int kvm_sm100_ipc_close(void* peer_ptr);
+
+/* Count exchange of one call (epoch = 1, 2, ... per call, same on all ranks):
+ * publishes this rank's per-expert counts (offsets [E+1] from
+ * kvm_sm100_moe_permute), waits (bounded) for every rank's, and writes
+ * local_offsets [E/world + 1] (group offsets of this rank's experts in its
+ * receive buffer: expert-major, then source-rank-major) and send_base [E]
+ * (first row of this rank's pairs of expert e in the owner's buffer). */
+int kvm_sm100_ep_counts(const kvm_ep_peers* peers, const int32_t* offsets,
+                        int32_t* send_base, int32_t* local_offsets,
+                        uint32_t epoch, kvm_stream_t stream);
+
+/* The dispatch all-to-all fused with the token scatter: row x[t] goes to
+ * recv[owner(e)][send_base[e] + pos[t*k+j] - offsets[e]] for each pair, by
+ * peer stores; then raises the data-ready flags. `done` is a zeroed uint32 in
+ * this rank's device memory. */
+int kvm_sm100_ep_dispatch(const kvm_ep_peers* peers, const void* x,
+                          const int32_t* topk_idx, const int32_t* pos,
+                          const int32_t* offsets, const int32_t* send_base, int T,
+                          int64_t cap_rows, uint32_t* done, uint32_t epoch,
+                          kvm_stream_t stream);
+
+/* Bounded wait for every rank's flag `slot` (1 data, 2 outputs) to reach
+ * epoch; raise this rank's flag `slot` on every rank. */
+int kvm_sm100_ep_wait(const kvm_ep_peers* peers, int slot, uint32_t epoch,
+                      kvm_stream_t stream);
+int kvm_sm100_ep_signal(const kvm_ep_peers* peers, int slot, uint32_t epoch,
+                        kvm_stream_t stream);
+
+/* The combine all-to-all fused with the weighted combine: out[t] =
+ * bf16(sum_j w[t,j] * y[owner][row of pair (t,j)]) by peer loads, fp32 with one
+ * fused multiply-add per slot in slot order (bit-identical to
+ * kvm_sm100_moe_combine on the same expert outputs). */
+int kvm_sm100_ep_combine(const kvm_ep_peers* peers, const int32_t* topk_idx,
+                         const int32_t* pos, const int32_t* offsets,
+                         const int32_t* send_base, const float* topk_w, void* out,
+                         int T, int64_t cap_rows, kvm_stream_t stream);
+
 /* ---------------------------------------------------------------- FP8 --- */
 
 /* FP8 e4m3 W8A8 GEMM with 128x128 fp32 block scales, bf16 output:

@@ -63,6 +63,16 @@ SIGNATURES = {
     "kvm_sm100_moe_scatter_rows": (_I, [_P, _P, _P, _I, _I, _I, _P]),
     "kvm_sm100_grouped_gemm_bf16": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, _I, _P]),
     "kvm_sm100_moe_combine": (_I, [_P, _P, _P, _P, _I, _I, _I, _P]),
+    "kvm_sm100_ipc_alloc": (_I, [_I64, C.POINTER(C.c_void_p)]),
+    "kvm_sm100_ipc_free": (_I, [_P]),
+    "kvm_sm100_ipc_get_handle": (_I, [_P, _P]),
+    "kvm_sm100_ipc_open_handle": (_I, [_P, C.POINTER(C.c_void_p)]),
+    "kvm_sm100_ipc_close": (_I, [_P]),
+    "kvm_sm100_ep_counts": (_I, [_P, _P, _P, _P, C.c_uint32, _P]),
+    "kvm_sm100_ep_dispatch": (_I, [_P, _P, _P, _P, _P, _P, _I, _I64, _P, C.c_uint32, _P]),
+    "kvm_sm100_ep_wait": (_I, [_P, _I, C.c_uint32, _P]),
+    "kvm_sm100_ep_signal": (_I, [_P, _I, C.c_uint32, _P]),
+    "kvm_sm100_ep_combine": (_I, [_P, _P, _P, _P, _P, _P, _P, _I, _I64, _P]),
     "kvm_sm100_gemm_fp8_blockscaled": (_I, [_P, _P, _P, _P, _P, _I64, _I, _I, _I, _P]),
     "kvm_sm100_quantize_e4m3_block128": (_I, [_P, _I, _P, _P, _I, _I, _P]),
     "kvm_sm100_transpose_u8": (_I, [_P, _P, _I, _I, _P]),
@@ -70,6 +80,18 @@ SIGNATURES = {
     "kvm_sm100_rmsnorm_bf16": (_I, [_P, _P, _P, _I, _I, _F, _P]),
     "kvm_sm100_silu_mul_bf16": (_I, [_P, _P, _P, _I64, _P]),
 }
+
+KVM_EP_MAX_RANKS = 8
+
+
+class EpPeers(C.Structure):
+    """Mirror of struct kvm_ep_peers (include/kvm_sm100.h)."""
+    _fields_ = [("rank", C.c_int32), ("world", C.c_int32), ("E", C.c_int32),
+                ("H", C.c_int32), ("k", C.c_int32), ("pad_", C.c_int32),
+                ("recv", C.c_void_p * KVM_EP_MAX_RANKS), ("y", C.c_void_p * KVM_EP_MAX_RANKS),
+                ("cnt", C.c_void_p * KVM_EP_MAX_RANKS),
+                ("flags", C.c_void_p * KVM_EP_MAX_RANKS)]
+
 
 _lib: C.CDLL | None = None
 

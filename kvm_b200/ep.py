@@ -1,5 +1,8 @@
 """Expert-parallel MoE layer: experts sharded over the ranks of a process
-group, token rows exchanged with NCCL point-to-point messages.
+group. Two exchanges are provided: ExpertParallelMoE (peer memory over NVLink,
+no host synchronisation, the production path) and ExpertParallelMoENccl
+(torch.distributed point-to-point messages; runs on gloo too, so its exchange
+logic is tested on CPU ranks).
 
 This executes `kernel.comm.moe_dispatch` / `kernel.comm.moe_combine` with
 their `ranks` operand (src/ir/dialect/kernel/ops.h:87-88, carried onto the
@@ -138,10 +141,13 @@ class CudaCompute:
         return self.out[:T]
 
 
-class ExpertParallelMoE:
-    """MoE layer with E/P experts per rank (weak scaling: each rank brings its
-    own tokens). `w13`/`w2` may be the full [E, ...] weights (this rank's slice
-    is taken) or already the local [E/P, ...] slice."""
+class ExpertParallelMoENccl:
+    """MoE layer with E/P experts per rank over torch.distributed point-to-point
+    messages (NCCL on GPUs, gloo on CPU). The host plans the messages from the
+    exchanged counts, which costs one device->host synchronisation per call;
+    ExpertParallelMoE below is the synchronisation-free NVLink path. `w13`/`w2`
+    may be the full [E, ...] weights (this rank's slice is taken) or already the
+    local [E/P, ...] slice."""
 
     def __init__(self, w_router, w13, w2, *, top_k: int, max_tokens: int, rank: int,
                  world: int, group=None, compute=None):
@@ -204,3 +210,143 @@ class ExpertParallelMoE:
         # reverse: what was received from (peer, row) goes back to (peer, row)
         self._exchange(y, c.yback, plan.recv, plan.send)
         return c.combine_local(T)
+
+
+class ExpertParallelMoE:
+    """Expert-parallel MoE layer over NVLink peer memory (one process per GPU).
+
+    Buffers that peers touch (receive rows, expert outputs, count matrix,
+    flags) are allocated with kvm_sm100_ipc_alloc and mapped into every rank
+    through CUDA IPC handles exchanged over the process group once, at
+    construction. A call launches 12 kernels on the current stream and never
+    synchronises with the host: route, permute (local), count exchange,
+    dispatch (peer stores), wait, grouped GEMMs, signal, wait, combine (peer
+    loads). Weak scaling: each rank brings `max_tokens` tokens at most.
+    """
+
+    LAUNCHES_PER_CALL = 12
+
+    def __init__(self, w_router, w13, w2, *, top_k: int, max_tokens: int, rank: int,
+                 world: int, group=None):
+        import ctypes as C
+        from ._lib import EpPeers, call, lib
+        E, H = w_router.shape
+        if E % world or world > 8:
+            raise ValueError(f"{E} experts over {world} ranks (at most 8)")
+        self.E, self.H, self.k, self.rank, self.world = E, H, top_k, rank, world
+        self.epr = E // world
+        e0 = rank * self.epr
+        if w13.shape[0] == E:
+            w13 = w13[e0:e0 + self.epr].contiguous()
+            w2 = w2[e0:e0 + self.epr].contiguous()
+        self.w_router, self.w13, self.w2 = w_router, w13, w2
+        self.F = w13.shape[1] // 2
+        self.group = group
+        dev = w_router.device
+        T, k = max_tokens, top_k
+        self.max_tokens = T
+        self.cap = T * k * world
+        i32 = torch.int32
+        self.logits = torch.empty((T, E), dtype=torch.float32, device=dev)
+        self.idx = torch.empty((T, k), dtype=i32, device=dev)
+        self.topw = torch.empty((T, k), dtype=torch.float32, device=dev)
+        self.offsets = torch.empty(E + 1, dtype=i32, device=dev)
+        self.pos = torch.empty(T * k, dtype=i32, device=dev)
+        self.src = torch.empty(T * k, dtype=i32, device=dev)
+        ws = int(lib().kvm_sm100_moe_permute_workspace(T, k, E))
+        self.ws = torch.empty(max(ws, 16), dtype=torch.uint8, device=dev)
+        self.send_base = torch.empty(E, dtype=i32, device=dev)
+        self.loc_off = torch.empty(self.epr + 1, dtype=i32, device=dev)
+        self.done = torch.zeros(1, dtype=i32, device=dev)
+        self.h = torch.empty((self.cap, self.F), dtype=torch.bfloat16, device=dev)
+        self.out = torch.empty((T, H), dtype=torch.bfloat16, device=dev)
+        sizes = {"recv": self.cap * H * 2, "y": self.cap * H * 2,
+                 "cnt": world * E * 4, "flags": 3 * world * 4}
+        self._own = {}
+        for name, nbytes in sizes.items():
+            p = C.c_void_p()
+            call("kvm_sm100_ipc_alloc", nbytes, C.byref(p))
+            self._own[name] = p.value
+        handles = {}
+        for name, p in self._own.items():
+            buf = C.create_string_buffer(64)
+            call("kvm_sm100_ipc_get_handle", p, buf)
+            handles[name] = buf.raw
+        gathered = [None] * world
+        if world > 1:
+            dist.all_gather_object(gathered, handles, group=group)
+        else:
+            gathered = [handles]
+        self._opened = []
+        peers = EpPeers()
+        peers.rank, peers.world, peers.E, peers.H, peers.k = rank, world, E, H, k
+        for r in range(world):
+            for name in sizes:
+                if r == rank:
+                    ptr = self._own[name]
+                else:
+                    q = C.c_void_p()
+                    call("kvm_sm100_ipc_open_handle", C.create_string_buffer(
+                        gathered[r][name], 64), C.byref(q))
+                    ptr = q.value
+                    self._opened.append(ptr)
+                getattr(peers, name)[r] = ptr
+        self.peers = peers
+        self._peers_ref = C.byref(peers)
+        self.epoch = 0
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier(group=group)
+
+    def __call__(self, x, probe=None):
+        from ._lib import call
+        T, H = x.shape
+        if H != self.H or T > self.max_tokens or T <= 0:
+            raise ValueError(f"x must be [T <= {self.max_tokens}, {self.H}]")
+        if x.dtype != torch.bfloat16 or not x.is_cuda or not x.is_contiguous():
+            raise ValueError("x must be a contiguous bf16 CUDA tensor")
+        self.epoch += 1
+        ep, pr = self.epoch, self._peers_ref
+        st = torch.cuda.current_stream().cuda_stream
+        E, k, F = self.E, self.k, self.F
+        call("kvm_sm100_moe_router_topk", x.data_ptr(), self.w_router.data_ptr(),
+             self.logits.data_ptr(), self.idx.data_ptr(), self.topw.data_ptr(),
+             T, H, E, k, st)
+        call("kvm_sm100_moe_permute", self.idx.data_ptr(), T, k, E, self.offsets.data_ptr(),
+             self.pos.data_ptr(), self.src.data_ptr(), self.ws.data_ptr(), st)
+        call("kvm_sm100_ep_counts", pr, self.offsets.data_ptr(), self.send_base.data_ptr(),
+             self.loc_off.data_ptr(), ep, st)
+        call("kvm_sm100_ep_dispatch", pr, x.data_ptr(), self.idx.data_ptr(),
+             self.pos.data_ptr(), self.offsets.data_ptr(), self.send_base.data_ptr(), T,
+             self.cap, self.done.data_ptr(), ep, st)
+        call("kvm_sm100_ep_wait", pr, 1, ep, st)
+        if probe is not None:
+            probe[0].record()
+        recv, y = self._own["recv"], self._own["y"]
+        call("kvm_sm100_grouped_gemm_bf16", recv, self.w13.data_ptr(), self.h.data_ptr(),
+             self.loc_off.data_ptr(), self.epr, self.cap, 2 * F, H, 2, st)
+        if probe is not None:
+            probe[1].record()
+        call("kvm_sm100_grouped_gemm_bf16", self.h.data_ptr(), self.w2.data_ptr(), y,
+             self.loc_off.data_ptr(), self.epr, self.cap, H, F, 0, st)
+        call("kvm_sm100_ep_signal", pr, 2, ep, st)
+        call("kvm_sm100_ep_wait", pr, 2, ep, st)
+        call("kvm_sm100_ep_combine", pr, self.idx.data_ptr(), self.pos.data_ptr(),
+             self.offsets.data_ptr(), self.send_base.data_ptr(), self.topw.data_ptr(),
+             self.out.data_ptr(), T, self.cap, st)
+        return self.out[:T]
+
+    def close(self):
+        """Unmap peer buffers and free this rank's (collective: all ranks call it)."""
+        from ._lib import call
+        torch.cuda.synchronize()
+        if self.world > 1:
+            dist.barrier(group=self.group)
+        for p in self._opened:
+            call("kvm_sm100_ipc_close", p)
+        self._opened = []
+        if self.world > 1:
+            dist.barrier(group=self.group)
+        for p in self._own.values():
+            call("kvm_sm100_ipc_free", p)
+        self._own = {}

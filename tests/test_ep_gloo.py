@@ -13,7 +13,7 @@ import torch.distributed as dist
 import torch.multiprocessing as mp
 
 import oracle
-from kvm_b200.ep import ExpertParallelMoE, make_plan
+from kvm_b200.ep import ExpertParallelMoENccl, make_plan
 
 T, H, E, F, K = 48, 64, 8, 128, 2
 
@@ -74,7 +74,7 @@ def _worker(rank, world, port, outdir):
         sl = slice(rank * epr, (rank + 1) * epr)
         comp = OracleCompute(wr, np.ascontiguousarray(w13[sl]),
                              np.ascontiguousarray(w2[sl]), world)
-        layer = ExpertParallelMoE(_i16(wr), _i16(w13), _i16(w2), top_k=K, max_tokens=T,
+        layer = ExpertParallelMoENccl(_i16(wr), _i16(w13), _i16(w2), top_k=K, max_tokens=T,
                                   rank=rank, world=world, compute=comp)
         out = layer(_i16(_tokens(rank)))
         np.save(os.path.join(outdir, f"out{rank}.npy"), out.numpy())

@@ -45,10 +45,11 @@ def _worker(rank, world, port, outdir):
     try:
         wr, w13, w2 = _make(dev)
         layer = ExpertParallelMoE(wr, w13, w2, top_k=K, max_tokens=T, rank=rank, world=world)
-        for _ in range(2):   # second call reuses every buffer
+        for _ in range(3):   # later calls reuse every buffer (epochs 2, 3)
             out = layer(_tokens(rank, dev))
         ops.device_status()
         torch.save(out.cpu(), os.path.join(outdir, f"out{rank}.pt"))
+        layer.close()
     finally:
         dist.destroy_process_group()
 
@@ -74,3 +75,20 @@ def test_expert_parallel_matches_single_gpu(world):
     ref = MoELayer(wr, w13, w2, K, T * world)(x).cpu()
     got = torch.cat(outs)
     assert torch.equal(got.view(torch.int16), ref.view(torch.int16))
+
+
+def test_expert_parallel_single_rank_matches_layer(cuda):
+    """world = 1 runs every exchange kernel (flags, counts, dispatch, combine)
+    on one GPU; no kernel waits on a concurrently running one."""
+    from kvm_b200.ep import ExpertParallelMoE
+    from kvm_b200.moe import MoELayer
+    from kvm_b200 import ops
+    wr, w13, w2 = _make(cuda)
+    x = _tokens(0, cuda)
+    ref = MoELayer(wr, w13, w2, K, T)(x).clone()
+    layer = ExpertParallelMoE(wr, w13, w2, top_k=K, max_tokens=T, rank=0, world=1)
+    for _ in range(3):
+        out = layer(x)
+    ops.device_status()
+    assert torch.equal(out.view(torch.int16), ref.view(torch.int16))
+    layer.close()
