@@ -273,6 +273,66 @@ int kvm_sm100_rmsnorm_bf16(const void* x, const void* gamma, void* y,
 int kvm_sm100_silu_mul_bf16(const void* g, const void* u, void* h, int64_t n,
                             kvm_stream_t stream);
 
+/* ------------------------------------------------ graph execution helpers --- */
+
+/* Element types of the elementwise interpreter and kvm_sm100_moe_topk. */
+enum kvm_ew_dtype { KVM_EW_BF16 = 0, KVM_EW_F32 = 1, KVM_EW_F16 = 2, KVM_EW_I32 = 3 };
+
+/* Instructions of the elementwise interpreter (one fp32 register file per
+ * element). LOAD reads input `a` at ((i / in_div[a]) mod in_size[a]) for output
+ * element i, which broadcasts an input over leading dimensions (in_div 1) and
+ * over trailing dimensions (in_div = their product); binary ops read
+ * registers a, b. */
+enum kvm_ew_op {
+  KVM_EW_LOAD = 0, KVM_EW_ADD, KVM_EW_SUB, KVM_EW_MUL, KVM_EW_DIV, KVM_EW_MAX,
+  KVM_EW_MIN, KVM_EW_NEG, KVM_EW_EXP, KVM_EW_LOG, KVM_EW_SQRT, KVM_EW_RSQRT,
+  KVM_EW_ABS, KVM_EW_RCP, KVM_EW_CMP_EQ, KVM_EW_CMP_NE, KVM_EW_CMP_LT,
+  KVM_EW_CMP_LE, KVM_EW_CMP_GT, KVM_EW_CMP_GE, KVM_EW_ROUND_BF16,
+  KVM_EW_ROUND_F16, KVM_EW_TRUNC_I32
+};
+
+#define KVM_EW_MAX_INPUTS 8
+#define KVM_EW_MAX_INSTR 32
+#define KVM_EW_MAX_REGS 16
+typedef struct kvm_ew_program {
+  int32_t n_inputs, n_instr, out_reg, out_dtype;
+  int32_t in_dtype[KVM_EW_MAX_INPUTS];
+  int64_t in_size[KVM_EW_MAX_INPUTS]; /* element i reads (i / in_div) % in_size */
+  int64_t in_div[KVM_EW_MAX_INPUTS];  /* 1 = broadcast over leading dims only */
+  uint8_t op[KVM_EW_MAX_INSTR], a[KVM_EW_MAX_INSTR], b[KVM_EW_MAX_INSTR],
+      dst[KVM_EW_MAX_INSTR];
+} kvm_ew_program;
+typedef struct kvm_ew_inputs {
+  const void* ptr[KVM_EW_MAX_INPUTS];
+} kvm_ew_inputs;
+
+/* out[i] = program(inputs) for i < n, converted to out_dtype (bf16/f16 RNE).
+ * Executes the kernel dialect's elementwise ops (add sub mul div max min neg
+ * exp log sqrt rsqrt abs, cmp.*, cast.*: src/ir/dialect/kernel/dialect.cpp:43-55)
+ * as lowered to task.alu.* / task.sfu.* (task/dialect.cpp:36-51). */
+int kvm_sm100_elementwise(const kvm_ew_program* program,
+                          const kvm_ew_inputs* inputs, void* out, int64_t n,
+                          kvm_stream_t stream);
+
+/* y[m] = sum_k A[m, k] * x[k] (fp32 accumulation), y of out_dtype (KVM_BF16 /
+ * KVM_F32): kernel.matmul with a [K, 1] right operand (e.g. the row means of
+ * the RMSNorm composite), whose [M, 1] result rows are too narrow for the
+ * tensor-core GEMM's 16-byte row stores. A, x bf16. */
+int kvm_sm100_gemv_bf16(const void* A, int64_t lda, const void* x, void* y,
+                        int out_dtype, int M, int K, kvm_stream_t stream);
+
+/* Softmax + top-k over router logits [T, E] of type logits_dtype
+ * (KVM_EW_F32 / KVM_EW_BF16) that a graph computed itself: the routing step of
+ * kernel.comm.moe_dispatch(x, g) (kernel/dialect.cpp:65). Same selection and
+ * weights as kvm_sm100_moe_router_topk. */
+int kvm_sm100_moe_topk(const void* logits, int logits_dtype, int T, int E, int k,
+                       int32_t* topk_idx, float* topk_w, kvm_stream_t stream);
+
+/* Seeded N(mean, std^2) fill of n elements of `dtype` (kvm_ew_dtype), from a
+ * counter-based hash of (seed, index), for synthetic graph inputs. */
+int kvm_sm100_fill_normal(void* out, int dtype, int64_t n, uint64_t seed,
+                          float mean, float std, kvm_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

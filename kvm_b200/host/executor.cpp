@@ -1,0 +1,521 @@
+// Executor implementation: task graph -> launch plan over the sm_100a C ABI.
+#include "executor.h"
+
+#include <any>
+#include <cstring>
+#include <stdexcept>
+#include <string>
+
+#include "dialect/kernel/ops.h"
+#include "dialect/task/values.h"
+#include "kvm_sm100.h"
+#include "node.h"
+#include "transform/kernel_to_task/kernel_to_task.h"
+
+namespace kvm::sm100 {
+namespace {
+
+using ir::dialect::Dtype;
+
+[[noreturn]] void Fail(const std::string& msg) {
+  throw std::runtime_error("kvm executor: " + msg);
+}
+
+void Check(int rc, const char* what) {
+  if (rc != KVM_OK)
+    Fail(std::string(what) + ": " + kvm_sm100_last_error());
+}
+
+int EwDtype(Dtype d) {
+  switch (d) {
+    case Dtype::kBf16: return KVM_EW_BF16;
+    case Dtype::kF16: return KVM_EW_F16;
+    case Dtype::kI32: return KVM_EW_I32;
+    case Dtype::kF32: return KVM_EW_F32;
+    default: Fail("dtype " + ir::dialect::DtypeName(d) + " is not executable");
+  }
+}
+
+const ir::task::TensorImpl& TaskTensorOf(const ir::ValueNode* v) {
+  const auto* t = v->value().impl.as<ir::task::TensorImpl>();
+  if (!t) Fail("value %" + v->value().name + " is not a task tensor");
+  return *t;
+}
+
+std::string OpKey(const ir::OpNode* op) {
+  const ir::Operator& o = op->op().op;
+  return o.dialect.empty() ? o.name : o.dialect + "." + o.name;
+}
+
+bool StartsWith(const std::string& s, const char* p) { return s.rfind(p, 0) == 0; }
+
+// Numpy-style broadcast of `in` to `out` as the interpreter's (size, div): the
+// input's non-1 dimensions, right-aligned, must be one contiguous run of the
+// output's dimensions; size = their product, div = product of the output
+// dimensions after them.
+void Broadcast(const std::vector<int64_t>& in, const std::vector<int64_t>& out,
+               int64_t* size, int64_t* div) {
+  const std::size_t r = out.size();
+  if (in.size() > r) Fail("elementwise operand has more dimensions than the result");
+  std::vector<int64_t> s(r, 1);
+  for (std::size_t i = 0; i < in.size(); ++i) s[r - in.size() + i] = in[i];
+  int first = -1, last = -1;
+  for (std::size_t d = 0; d < r; ++d) {
+    if (s[d] != 1 && s[d] != out[d]) Fail("elementwise operand does not broadcast");
+    if (s[d] != 1) {
+      if (first < 0) first = int(d);
+      else if (last != int(d) - 1) Fail("unsupported broadcast pattern");
+      last = int(d);
+    }
+  }
+  *size = 1;
+  *div = 1;
+  if (first < 0) return;  // scalar
+  for (int d = first; d <= last; ++d) *size *= out[d];
+  for (std::size_t d = last + 1; d < r; ++d) *div *= out[d];
+}
+
+}  // namespace
+
+int64_t DtypeBytes(Dtype d) {
+  switch (d) {
+    case Dtype::kI16: case Dtype::kF16: case Dtype::kBf16: return 2;
+    case Dtype::kBool: return 1;
+    default: return 4;
+  }
+}
+
+int64_t Buffer::numel() const {
+  int64_t n = 1;
+  for (int64_t s : shape) n *= s;
+  return n;
+}
+
+int64_t Buffer::bytes() const { return numel() * DtypeBytes(dtype); }
+
+struct Executor::Routing {
+  int T = 0, E = 0, k = 0;
+  int32_t* idx = nullptr;
+  float* w = nullptr;
+  int32_t* offsets = nullptr;
+  int32_t* pos = nullptr;
+  int32_t* src = nullptr;
+  void* ws = nullptr;
+};
+
+struct Executor::Slot {
+  enum Kind { kGlobal, kView, kMma, kExpr } kind = kGlobal;
+  Buffer buf;                             // kGlobal
+  const ir::ValueNode* base = nullptr;    // kView: the viewed global value
+  std::vector<const ir::ValueNode*> args; // kMma (a, b[, c]) / kExpr operands
+  std::string op;                         // kExpr: "alu.add", "sfu.exp", ...
+  Routing* group = nullptr;               // rows grouped by a moe_dispatch
+};
+
+Executor::Executor(const ir::Graph& kernel, const ir::AttrMap& attrs)
+    : kernel_(kernel), attrs_(attrs) {
+  transform::TransformKernelToTask(kernel_, task_);
+  for (const ir::ValueNode* a : task_.root()->arguments()) {
+    const auto& t = TaskTensorOf(a);
+    Buffer b;
+    b.shape.assign(t.shape.begin(), t.shape.end());
+    b.dtype = t.dtype;
+    inputs_.push_back(b);
+    input_names_.push_back(a->value().name);
+  }
+}
+
+Executor::~Executor() {
+  for (void* p : allocations_) cudaFree(p);
+}
+
+void* Executor::Alloc(int64_t bytes) {
+  void* p = nullptr;
+  if (cudaMalloc(&p, static_cast<size_t>(bytes > 0 ? bytes : 16)) != cudaSuccess)
+    Fail("cudaMalloc of " + std::to_string(bytes) + " bytes failed");
+  allocations_.push_back(p);
+  return p;
+}
+
+Executor::Slot& Executor::slot(const ir::ValueNode* v) {
+  auto it = slots_.find(v);
+  if (it == slots_.end()) Fail("value %" + v->value().name + " has no producer");
+  return *it->second;
+}
+
+const Buffer& Executor::GlobalOf(const ir::ValueNode* v) {
+  Slot* s = &slot(v);
+  while (s->kind == Slot::kView) s = &slot(s->base);
+  if (s->kind != Slot::kGlobal)
+    Fail("value %" + v->value().name + " is read before it is stored");
+  return s->buf;
+}
+
+Buffer& Executor::Materialize(const ir::ValueNode* v) {
+  const auto& t = TaskTensorOf(v);
+  auto s = std::make_unique<Slot>();
+  s->kind = Slot::kGlobal;
+  s->buf.shape.assign(t.shape.begin(), t.shape.end());
+  s->buf.dtype = t.dtype;
+  s->buf.ptr = Alloc(s->buf.bytes());
+  Buffer& b = s->buf;
+  slots_[v] = std::move(s);
+  return b;
+}
+
+const ir::OpNode* Executor::KernelCommOp(const std::string& name, int nth) const {
+  int seen = 0;
+  for (const ir::OpNode* op : kernel_.root()->operations())
+    if (op->op().op.name == name && seen++ == nth) return op;
+  return nullptr;
+}
+
+void Executor::Prepare() {
+  if (prepared_) return;
+  const ir::Block* root = task_.root();
+  for (std::size_t i = 0; i < root->arguments().size(); ++i) {
+    inputs_[i].ptr = Alloc(inputs_[i].bytes());
+    auto s = std::make_unique<Slot>();
+    s->kind = Slot::kGlobal;
+    s->buf = inputs_[i];
+    slots_[root->arguments()[i]] = std::move(s);
+  }
+  for (const ir::OpNode* op : root->operations()) {
+    const std::string key = OpKey(op);
+    const ir::ValueNode* res = op->results().empty() ? nullptr : op->results()[0];
+    if (key == "task.tma.gmem_to_smem" || key == "task.lsu.gmem_to_reg" ||
+        key == "task.lsu.smem_to_reg") {
+      auto s = std::make_unique<Slot>();
+      s->kind = Slot::kView;
+      s->base = op->operands()[0];
+      s->group = slot(op->operands()[0]).group;
+      slots_[res] = std::move(s);
+    } else if (key == "task.tc.mma" || key == "task.tc.mma_acc") {
+      auto s = std::make_unique<Slot>();
+      s->kind = Slot::kMma;
+      s->args.assign(op->operands().begin(), op->operands().end());
+      s->group = slot(op->operands()[0]).group;
+      slots_[res] = std::move(s);
+    } else if (StartsWith(key, "task.alu.") || StartsWith(key, "task.sfu.")) {
+      auto s = std::make_unique<Slot>();
+      s->kind = Slot::kExpr;
+      s->op = key.substr(5);
+      s->args.assign(op->operands().begin(), op->operands().end());
+      for (const ir::ValueNode* a : s->args)
+        if (!s->group) s->group = slot(a).group;
+      slots_[res] = std::move(s);
+    } else if (key == "task.lsu.reg_to_gmem" || key == "task.tma.smem_to_gmem") {
+      PlanStore(op->operands()[0], res);
+    } else if (StartsWith(key, "task.comm.")) {
+      PlanComm(op);
+    } else {
+      Fail("no executor rule for task op '" + key + "'");
+    }
+  }
+  for (const ir::ValueNode* o : root->outputs()) outputs_.push_back(GlobalOf(o));
+  prepared_ = true;
+}
+
+void Executor::PlanStore(const ir::ValueNode* src, const ir::ValueNode* dst) {
+  Slot& s = slot(src);
+  Routing* group = s.group;
+  Buffer& out = Materialize(dst);
+  slot(dst).group = group;
+  if (s.kind == Slot::kMma) {
+    PlanGemm(src, out);
+  } else if (s.kind == Slot::kExpr) {
+    PlanExpr(src, out);
+  } else {
+    const Buffer in = GlobalOf(src);
+    if (in.bytes() != out.bytes()) Fail("store of %" + dst->value().name + ": size mismatch");
+    void* d = out.ptr;
+    const void* p = in.ptr;
+    const int64_t n = in.bytes();
+    steps_.push_back([d, p, n](cudaStream_t st) {
+      return cudaMemcpyAsync(d, p, n, cudaMemcpyDeviceToDevice, st) == cudaSuccess
+                 ? KVM_OK : KVM_ERR_CUDA;
+    });
+    step_names_.push_back("copy");
+  }
+}
+
+void Executor::PlanGemm(const ir::ValueNode* mma, const Buffer& out) {
+  Slot& s = slot(mma);
+  const Buffer A = GlobalOf(s.args[0]);
+  const Buffer B = GlobalOf(s.args[1]);
+  const Buffer* C = s.args.size() > 2 ? &GlobalOf(s.args[2]) : nullptr;
+  if (A.dtype != Dtype::kBf16 || B.dtype != Dtype::kBf16)
+    Fail("tcgen05 GEMM in this build takes bf16 operands (got " +
+         ir::dialect::DtypeName(A.dtype) + ", " + ir::dialect::DtypeName(B.dtype) + ")");
+  if (A.shape.size() != 2) Fail("GEMM A operand must be 2-D");
+  const int64_t M = A.shape[0], K = A.shape[1];
+  if (B.shape.size() == 2 && B.shape[1] == 1 && !C) {
+    if (B.shape[0] != K) Fail("GEMM inner dimensions disagree");
+    if (out.dtype != Dtype::kBf16 && out.dtype != Dtype::kF32)
+      Fail("GEMM result must be bf16 or f32");
+    const void* a = A.ptr; const void* b = B.ptr;
+    void* d = out.ptr;
+    const int od = out.dtype == Dtype::kF32 ? KVM_F32 : KVM_BF16;
+    steps_.push_back([=](cudaStream_t st) {
+      return kvm_sm100_gemv_bf16(a, K, b, d, od, int(M), int(K), st);
+    });
+    step_names_.push_back("gemv_bf16");
+    return;
+  }
+  if (B.shape.size() == 2) {
+    if (B.shape[0] != K) Fail("GEMM inner dimensions disagree");
+    const int64_t N = B.shape[1];
+    if (out.numel() != M * N) Fail("GEMM result shape disagrees with A.B");
+    if (out.dtype != Dtype::kBf16 && out.dtype != Dtype::kF32)
+      Fail("GEMM result must be bf16 or f32");
+    if (C && (C->dtype != out.dtype || C->numel() != out.numel()))
+      Fail("gemm addend C must match the result's dtype and shape");
+    const void* a = A.ptr; const void* b = B.ptr;
+    const void* c = C ? C->ptr : nullptr;
+    void* d = out.ptr;
+    const int od = out.dtype == Dtype::kF32 ? KVM_F32 : KVM_BF16;
+    steps_.push_back([=](cudaStream_t st) {
+      return kvm_sm100_gemm_bf16(a, K, b, N, KVM_B_KN, c, d, N, od, int(M), int(N),
+                                 int(K), st);
+    });
+    step_names_.push_back("gemm_bf16");
+    return;
+  }
+  if (B.shape.size() != 3) Fail("GEMM B operand must be 2-D or 3-D");
+  if (!s.group) Fail("a 3-D (per-expert) B needs A rows grouped by a moe_dispatch");
+  if (C) Fail("per-expert gemm with an addend is not supported");
+  const int64_t E = B.shape[0], N = B.shape[2];
+  if (B.shape[1] != K || E != s.group->E) Fail("per-expert B must be [E, K, N]");
+  if (out.dtype != Dtype::kBf16) Fail("per-expert GEMM result must be bf16");
+  // One-time re-layout of the expert weights [E, K, N] -> [E, N, K].
+  void* bt = Alloc(B.bytes());
+  const void* b = B.ptr;
+  once_steps_.push_back([=](cudaStream_t st) {
+    return kvm_sm100_transpose_bf16(b, bt, int(E), int(K), int(N), st);
+  });
+  Routing* r = s.group;
+  const void* a = A.ptr;
+  void* d = out.ptr;
+  steps_.push_back([=](cudaStream_t st) {
+    return kvm_sm100_grouped_gemm_bf16(a, bt, d, r->offsets, int(E), int(M), int(N),
+                                       int(K), 0, st);
+  });
+  step_names_.push_back("grouped_gemm_bf16");
+}
+
+void Executor::PlanExpr(const ir::ValueNode* expr, const Buffer& out) {
+  kvm_ew_program prog;
+  std::memset(&prog, 0, sizeof(prog));
+  kvm_ew_inputs ins;
+  std::memset(&ins, 0, sizeof(ins));
+  std::unordered_map<const void*, int> input_of;  // buffer -> input slot
+  std::unordered_map<const ir::ValueNode*, int> reg_of;
+  int next_reg = 0;
+  auto emit = [&](int op, int a, int b) {
+    if (prog.n_instr >= KVM_EW_MAX_INSTR || next_reg >= KVM_EW_MAX_REGS)
+      Fail("elementwise expression too large");
+    const int s = prog.n_instr++;
+    prog.op[s] = uint8_t(op);
+    prog.a[s] = uint8_t(a);
+    prog.b[s] = uint8_t(b);
+    prog.dst[s] = uint8_t(next_reg);
+    return next_reg++;
+  };
+  std::function<int(const ir::ValueNode*)> gen = [&](const ir::ValueNode* v) -> int {
+    auto it = reg_of.find(v);
+    if (it != reg_of.end()) return it->second;
+    Slot& s = slot(v);
+    int r;
+    if (s.kind != Slot::kExpr) {
+      const Buffer& b = GlobalOf(v);
+      auto in = input_of.find(b.ptr);
+      int slot_i;
+      if (in == input_of.end()) {
+        if (prog.n_inputs >= KVM_EW_MAX_INPUTS) Fail("elementwise: too many inputs");
+        slot_i = prog.n_inputs++;
+        ins.ptr[slot_i] = b.ptr;
+        prog.in_dtype[slot_i] = EwDtype(b.dtype);
+        Broadcast(b.shape, out.shape, &prog.in_size[slot_i], &prog.in_div[slot_i]);
+        input_of[b.ptr] = slot_i;
+      } else {
+        slot_i = in->second;
+      }
+      r = emit(KVM_EW_LOAD, slot_i, 0);
+    } else {
+      const std::string& op = s.op;
+      // a * (1 / b) as lowered for kernel.div is the division a / b.
+      if (op == "alu.mul" && slot(s.args[1]).kind == Slot::kExpr &&
+          slot(s.args[1]).op == "sfu.rcp") {
+        const int a = gen(s.args[0]);
+        const int b = gen(slot(s.args[1]).args[0]);
+        r = emit(KVM_EW_DIV, a, b);
+      } else {
+        static const std::unordered_map<std::string, int> kOps = {
+            {"alu.add", KVM_EW_ADD}, {"alu.sub", KVM_EW_SUB}, {"alu.mul", KVM_EW_MUL},
+            {"alu.max", KVM_EW_MAX}, {"alu.min", KVM_EW_MIN}, {"alu.neg", KVM_EW_NEG},
+            {"alu.abs", KVM_EW_ABS}, {"sfu.rcp", KVM_EW_RCP}, {"sfu.exp", KVM_EW_EXP},
+            {"sfu.log", KVM_EW_LOG}, {"sfu.sqrt", KVM_EW_SQRT},
+            {"sfu.rsqrt", KVM_EW_RSQRT}, {"alu.cmp.eq", KVM_EW_CMP_EQ},
+            {"alu.cmp.ne", KVM_EW_CMP_NE}, {"alu.cmp.lt", KVM_EW_CMP_LT},
+            {"alu.cmp.le", KVM_EW_CMP_LE}, {"alu.cmp.gt", KVM_EW_CMP_GT},
+            {"alu.cmp.ge", KVM_EW_CMP_GE}, {"alu.cast.bf16", KVM_EW_ROUND_BF16},
+            {"alu.cast.f16", KVM_EW_ROUND_F16}, {"alu.cast.i32", KVM_EW_TRUNC_I32},
+            {"alu.cast.f32", -1}};
+        auto k = kOps.find(op);
+        if (k == kOps.end()) Fail("no elementwise rule for task op '" + op + "'");
+        const int a = gen(s.args[0]);
+        const int b = s.args.size() > 1 ? gen(s.args[1]) : 0;
+        r = k->second < 0 ? a : emit(k->second, a, b);
+      }
+    }
+    reg_of[v] = r;
+    return r;
+  };
+  prog.out_reg = gen(expr);
+  prog.out_dtype = EwDtype(out.dtype);
+  void* d = out.ptr;
+  const int64_t n = out.numel();
+  for (int i = 0; i < prog.n_inputs; ++i)
+    if (n % (prog.in_size[i] * prog.in_div[i]) != 0)
+      Fail("elementwise operand does not broadcast to the result shape");
+  steps_.push_back([prog, ins, d, n](cudaStream_t st) {
+    return kvm_sm100_elementwise(&prog, &ins, d, n, st);
+  });
+  step_names_.push_back("elementwise");
+}
+
+void Executor::PlanComm(const ir::OpNode* op) {
+  const std::string name = op->op().op.name;  // "comm.moe_dispatch", ...
+  int nth = 0;
+  for (const ir::OpNode* o : task_.root()->operations()) {
+    if (o == op) break;
+    if (o->op().op.name == name) ++nth;
+  }
+  const ir::OpNode* kop = KernelCommOp(name, nth);
+  const ir::ValueNode* res = op->results()[0];
+  if (name == "comm.moe_dispatch") {
+    const Buffer x = GlobalOf(op->operands()[0]);
+    const Buffer g = GlobalOf(op->operands()[1]);
+    if (x.shape.size() != 2 || g.shape.size() != 2 || g.shape[0] != x.shape[0])
+      Fail("moe_dispatch(x [T,H], g [T,E]) shapes disagree");
+    if (x.dtype != Dtype::kBf16) Fail("moe_dispatch tokens must be bf16");
+    int k = 2;
+    if (kop)
+      if (const std::any* a = attrs_.Get(kop, "top_k"))
+        if (const auto* v = std::any_cast<std::int64_t>(a)) k = int(*v);
+    auto r = std::make_unique<Routing>();
+    r->T = int(x.shape[0]);
+    r->E = int(g.shape[1]);
+    r->k = k;
+    const int64_t n = int64_t(r->T) * k;
+    r->idx = static_cast<int32_t*>(Alloc(n * 4));
+    r->w = static_cast<float*>(Alloc(n * 4));
+    r->offsets = static_cast<int32_t*>(Alloc((r->E + 1) * 4));
+    r->pos = static_cast<int32_t*>(Alloc(n * 4));
+    r->src = static_cast<int32_t*>(Alloc(n * 4));
+    r->ws = Alloc(kvm_sm100_moe_permute_workspace(r->T, k, r->E));
+    Buffer& out = Materialize(res);
+    if (out.numel() != n * x.shape[1] || out.dtype != Dtype::kBf16)
+      Fail("moe_dispatch result must be bf16 [T*top_k, H]");
+    Routing* rp = r.get();
+    slot(res).group = rp;
+    const void* gp = g.ptr;
+    const int gd = EwDtype(g.dtype);
+    const void* xp = x.ptr;
+    void* dp = out.ptr;
+    const int H = int(x.shape[1]);
+    steps_.push_back([=](cudaStream_t st) {
+      return kvm_sm100_moe_topk(gp, gd, rp->T, rp->E, rp->k, rp->idx, rp->w, st);
+    });
+    step_names_.push_back("moe_topk");
+    steps_.push_back([=](cudaStream_t st) {
+      return kvm_sm100_moe_permute(rp->idx, rp->T, rp->k, rp->E, rp->offsets, rp->pos,
+                                   rp->src, rp->ws, st);
+    });
+    step_names_.push_back("moe_permute");
+    steps_.push_back([=](cudaStream_t st) {
+      return kvm_sm100_moe_scatter_rows(xp, rp->pos, dp, rp->T, rp->k, H, st);
+    });
+    step_names_.push_back("moe_scatter_rows");
+    routing_of_[g.ptr] = rp;
+    routings_.push_back(std::move(r));
+    return;
+  }
+  if (name == "comm.moe_combine") {
+    const Buffer y = GlobalOf(op->operands()[0]);
+    const Buffer g = GlobalOf(op->operands()[1]);
+    auto it = routing_of_.find(g.ptr);
+    if (it == routing_of_.end()) Fail("moe_combine(y, g): g was never dispatched on");
+    Routing* rp = it->second;
+    Buffer& out = Materialize(res);
+    const int H = int(y.shape.back());
+    if (out.numel() != int64_t(rp->T) * H || out.dtype != Dtype::kBf16)
+      Fail("moe_combine result must be bf16 [T, H]");
+    const void* yp = y.ptr;
+    void* op_ = out.ptr;
+    steps_.push_back([=](cudaStream_t st) {
+      return kvm_sm100_moe_combine(yp, rp->pos, rp->w, op_, rp->T, rp->k, H, st);
+    });
+    step_names_.push_back("moe_combine");
+    return;
+  }
+  // Collectives over a single rank are identities.
+  std::vector<int> ranks;
+  if (const auto* r = op->op().impl.as<ir::kernel::AllReduceSum>()) ranks = r->ranks;
+  if (const auto* r = op->op().impl.as<ir::kernel::AllReduceMax>()) ranks = r->ranks;
+  if (const auto* r = op->op().impl.as<ir::kernel::AllGather>()) ranks = r->ranks;
+  if (const auto* r = op->op().impl.as<ir::kernel::AllToAllOp>()) ranks = r->ranks;
+  if (ranks.size() > 1)
+    Fail("'" + name + "' over " + std::to_string(ranks.size()) +
+         " ranks runs through the multi-process runtime, not this single-GPU executor");
+  PlanStore(op->operands()[0], res);
+}
+
+void Executor::CopyInput(int index, const void* host, int64_t bytes) {
+  if (index < 0 || index >= int(inputs_.size())) Fail("input index out of range");
+  if (!prepared_) Prepare();
+  if (bytes != inputs_[index].bytes()) Fail("input " + input_names_[index] + ": byte count");
+  if (cudaMemcpy(inputs_[index].ptr, host, bytes, cudaMemcpyHostToDevice) != cudaSuccess)
+    Fail("input copy failed");
+}
+
+void Executor::FillInputNormal(int index, uint64_t seed, float mean, float std) {
+  if (!prepared_) Prepare();
+  const Buffer& b = inputs_.at(index);
+  Check(kvm_sm100_fill_normal(b.ptr, EwDtype(b.dtype), b.numel(), seed, mean, std,
+                              nullptr), "fill_normal");
+}
+
+void Executor::FillInputConst(int index, float value) {
+  if (!prepared_) Prepare();
+  const Buffer& b = inputs_.at(index);
+  void* scalar = Alloc(4);
+  if (cudaMemcpy(scalar, &value, 4, cudaMemcpyHostToDevice) != cudaSuccess)
+    Fail("constant copy failed");
+  kvm_ew_program prog;
+  std::memset(&prog, 0, sizeof(prog));
+  prog.n_inputs = 1;
+  prog.n_instr = 1;
+  prog.in_dtype[0] = KVM_EW_F32;
+  prog.in_size[0] = 1;
+  prog.in_div[0] = 1;
+  prog.out_dtype = EwDtype(b.dtype);
+  kvm_ew_inputs ins;
+  std::memset(&ins, 0, sizeof(ins));
+  ins.ptr[0] = scalar;
+  Check(kvm_sm100_elementwise(&prog, &ins, b.ptr, b.numel(), nullptr), "fill const");
+}
+
+int Executor::Run(cudaStream_t stream) {
+  if (!prepared_) Prepare();
+  if (!once_done_) {
+    for (auto& s : once_steps_)
+      if (int rc = s(stream); rc != KVM_OK) return rc;
+    once_done_ = true;
+  }
+  for (auto& s : steps_)
+    if (int rc = s(stream); rc != KVM_OK) return rc;
+  return KVM_OK;
+}
+
+}  // namespace kvm::sm100

@@ -1,0 +1,204 @@
+// kvm_run: execute a .kvm kernel-dialect graph on one B200.
+//
+//   kvm_run GRAPH.kvm [--inputs DIR] [--out DIR] [--seed S] [--warmup W]
+//                     [--iters N] [--dump-task] [--lower-only]
+//
+// The graph is parsed by the reference parser (serial::Parse), lowered by the
+// reference transform with the sm_100a Device target, and executed by the
+// Executor. Inputs: DIR/<arg>.bin (raw bytes of the declared dtype) when
+// given, else the argument's attrs -- {fill = v} for a constant,
+// {std = s} (and {mean = m}) for seeded normal values -- else N(0, 1) from
+// seed S + argument index. Outputs are written to DIR/<name>.bin; a JSON
+// summary (launch plan, time per run, output checksums) goes to stdout.
+#include <cuda_runtime.h>
+
+#include <any>
+#include <chrono>
+#include <cstdio>
+#include <cstring>
+#include <fstream>
+#include <iostream>
+#include <sstream>
+#include <string>
+#include <vector>
+
+#include "dialect/kernel/dialect.h"
+#include "dialect/task/dialect.h"
+#include "executor.h"
+#include "kvm_sm100.h"
+#include "serialization/parser.h"
+#include "serialization/registry.h"
+#include "serialization/serializer.h"
+
+namespace {
+
+std::string ReadFile(const std::string& path) {
+  std::ifstream f(path, std::ios::binary);
+  if (!f) throw std::runtime_error("cannot read " + path);
+  std::stringstream ss;
+  ss << f.rdbuf();
+  return ss.str();
+}
+
+bool ReadBin(const std::string& path, std::vector<char>& out) {
+  std::ifstream f(path, std::ios::binary);
+  if (!f) return false;
+  out.assign(std::istreambuf_iterator<char>(f), std::istreambuf_iterator<char>());
+  return true;
+}
+
+double AttrNumber(const kvm::ir::AttrMap& attrs, const kvm::ir::ValueNode* v,
+                  const char* key, bool* found) {
+  const std::any* a = attrs.Get(v, key);
+  *found = a != nullptr;
+  if (!a) return 0;
+  if (const auto* d = std::any_cast<double>(a)) return *d;
+  if (const auto* i = std::any_cast<std::int64_t>(a)) return double(*i);
+  *found = false;
+  return 0;
+}
+
+// Order-independent checksum: sum and sum of squares of the values as fp64.
+void Checksum(const kvm::sm100::Buffer& b, double* sum, double* sq) {
+  std::vector<char> host(b.bytes());
+  cudaMemcpy(host.data(), b.ptr, host.size(), cudaMemcpyDeviceToHost);
+  *sum = *sq = 0;
+  const int64_t n = b.numel();
+  for (int64_t i = 0; i < n; ++i) {
+    double v = 0;
+    switch (b.dtype) {
+      case kvm::ir::dialect::Dtype::kBf16: {
+        uint32_t u = uint32_t(reinterpret_cast<uint16_t*>(host.data())[i]) << 16;
+        float f;
+        std::memcpy(&f, &u, 4);
+        v = f;
+        break;
+      }
+      case kvm::ir::dialect::Dtype::kF32:
+        v = reinterpret_cast<float*>(host.data())[i];
+        break;
+      case kvm::ir::dialect::Dtype::kI32:
+        v = reinterpret_cast<int32_t*>(host.data())[i];
+        break;
+      default:
+        v = 0;
+    }
+    *sum += v;
+    *sq += v * v;
+  }
+}
+
+}  // namespace
+
+int main(int argc, char** argv) {
+  std::string graph_path, in_dir, out_dir;
+  uint64_t seed = 0;
+  int warmup = 1, iters = 1;
+  bool dump_task = false, lower_only = false;
+  for (int i = 1; i < argc; ++i) {
+    std::string a = argv[i];
+    auto next = [&]() -> std::string {
+      if (i + 1 >= argc) throw std::runtime_error("missing value for " + a);
+      return argv[++i];
+    };
+    if (a == "--inputs") in_dir = next();
+    else if (a == "--out") out_dir = next();
+    else if (a == "--seed") seed = std::stoull(next());
+    else if (a == "--warmup") warmup = std::stoi(next());
+    else if (a == "--iters") iters = std::stoi(next());
+    else if (a == "--dump-task") dump_task = true;
+    else if (a == "--lower-only") lower_only = true;
+    else if (graph_path.empty()) graph_path = a;
+    else throw std::runtime_error("unexpected argument " + a);
+  }
+  if (graph_path.empty()) {
+    std::cerr << "usage: kvm_run GRAPH.kvm [--inputs DIR] [--out DIR] [--seed S]"
+                 " [--warmup W] [--iters N] [--dump-task]\n";
+    return 2;
+  }
+  try {
+    kvm::ir::serial::Registry reg;
+    kvm::ir::kernel::RegisterKernelDialect(reg);
+    kvm::ir::Graph kernel;
+    kvm::ir::AttrMap attrs = kvm::ir::serial::Parse(ReadFile(graph_path), reg, kernel);
+    kvm::sm100::Executor ex(kernel, attrs);
+    if (dump_task) {
+      kvm::ir::serial::Registry treg;
+      kvm::ir::task::RegisterTaskDialect(treg);
+      std::cerr << kvm::ir::serial::Serialize(ex.task_graph(), treg);
+    }
+    if (lower_only) {  // parse + lower only: no GPU needed
+      std::cout << "{\"graph\": \"" << graph_path << "\", \"task_ops\": "
+                << ex.task_graph().root()->operations().size() << "}" << std::endl;
+      return 0;
+    }
+    ex.Prepare();
+    const auto& args = kernel.root()->arguments();
+    for (std::size_t i = 0; i < ex.inputs().size(); ++i) {
+      const std::string& name = ex.input_names()[i];
+      std::vector<char> data;
+      bool f_fill = false, f_std = false, f_mean = false;
+      const double fill = AttrNumber(attrs, args[i], "fill", &f_fill);
+      const double sd = AttrNumber(attrs, args[i], "std", &f_std);
+      const double mean = AttrNumber(attrs, args[i], "mean", &f_mean);
+      if (!in_dir.empty() && ReadBin(in_dir + "/" + name + ".bin", data))
+        ex.CopyInput(int(i), data.data(), int64_t(data.size()));
+      else if (f_fill)
+        ex.FillInputConst(int(i), float(fill));
+      else
+        ex.FillInputNormal(int(i), seed + i, float(mean), f_std ? float(sd) : 1.0f);
+    }
+    cudaStream_t st;
+    cudaStreamCreate(&st);
+    for (int w = 0; w < warmup; ++w)
+      if (int rc = ex.Run(st); rc != KVM_OK)
+        throw std::runtime_error(std::string("run: ") + kvm_sm100_last_error());
+    int status = 0;
+    if (kvm_sm100_device_status(&status, 1) != KVM_OK)
+      throw std::runtime_error(std::string("device: ") + kvm_sm100_last_error());
+    cudaEvent_t e0, e1;
+    cudaEventCreate(&e0);
+    cudaEventCreate(&e1);
+    cudaEventRecord(e0, st);
+    for (int it = 0; it < iters; ++it)
+      if (int rc = ex.Run(st); rc != KVM_OK)
+        throw std::runtime_error(std::string("run: ") + kvm_sm100_last_error());
+    cudaEventRecord(e1, st);
+    cudaEventSynchronize(e1);
+    float ms = 0;
+    cudaEventElapsedTime(&ms, e0, e1);
+    if (kvm_sm100_device_status(&status, 1) != KVM_OK)
+      throw std::runtime_error(std::string("device: ") + kvm_sm100_last_error());
+
+    std::ostringstream js;
+    js << "{\"graph\": \"" << graph_path << "\", \"launch_steps\": "
+       << ex.launches_per_run() << ", \"ms_per_run\": " << (iters ? ms / iters : 0)
+       << ", \"iters\": " << iters << ", \"steps\": [";
+    for (std::size_t i = 0; i < ex.step_names().size(); ++i)
+      js << (i ? ", " : "") << "\"" << ex.step_names()[i] << "\"";
+    js << "], \"outputs\": [";
+    const auto& outs = kernel.root()->outputs();
+    for (std::size_t i = 0; i < ex.outputs().size(); ++i) {
+      const auto& b = ex.outputs()[i];
+      const std::string name = outs[i]->value().name;
+      double sum, sq;
+      Checksum(b, &sum, &sq);
+      js << (i ? ", " : "") << "{\"name\": \"" << name << "\", \"numel\": " << b.numel()
+         << ", \"dtype\": \"" << kvm::ir::dialect::DtypeName(b.dtype)
+         << "\", \"sum\": " << sum << ", \"sumsq\": " << sq << "}";
+      if (!out_dir.empty()) {
+        std::vector<char> host(b.bytes());
+        cudaMemcpy(host.data(), b.ptr, host.size(), cudaMemcpyDeviceToHost);
+        std::ofstream f(out_dir + "/" + name + ".bin", std::ios::binary);
+        f.write(host.data(), std::streamsize(host.size()));
+      }
+    }
+    js << "]}";
+    std::cout << js.str() << std::endl;
+    cudaStreamDestroy(st);
+  } catch (const std::exception& e) {
+    std::cerr << "kvm_run: " << e.what() << std::endl;
+    return 1;
+  }
+  return 0;
+}
