@@ -273,6 +273,33 @@ int kvm_sm100_rmsnorm_bf16(const void* x, const void* gamma, void* y,
 int kvm_sm100_silu_mul_bf16(const void* g, const void* u, void* h, int64_t n,
                             kvm_stream_t stream);
 
+/* ---------------------------------------------------------- attention --- */
+
+/* Causal grouped-query attention over a batch of sequences (prefill):
+ * kernel.attn.prefill (src/ir/dialect/kernel/dialect.cpp:38) for equal-length
+ * sequences. Tokens are rows b*L + pos; q/out hold HQ heads of 128 columns
+ * each, k/v hold HKV heads (q head h reads kv head h / (HQ/HKV)); row strides
+ * ldq, ldk, ldv, ldo in elements (bf16). Per head:
+ *   S = scale * Q K^T (fp32), P = softmax over keys <= pos (fp32 statistics,
+ *   P rounded to bf16), O = P V (fp32 accumulate, bf16 out).
+ * scale <= 0 selects 1/sqrt(head_dim). head_dim must be 128, L % 8 == 0.
+ * workspace: kvm_sm100_attention_workspace(B, L, HQ, HKV) bytes. */
+int64_t kvm_sm100_attention_workspace(int B, int L, int HQ, int HKV);
+int kvm_sm100_attention_prefill_bf16(const void* q, int64_t ldq, const void* k,
+                                     int64_t ldk, const void* v, int64_t ldv,
+                                     void* out, int64_t ldo, int B, int L, int HQ,
+                                     int HKV, int head_dim, float scale,
+                                     void* workspace, int64_t workspace_bytes,
+                                     kvm_stream_t stream);
+
+/* Rotary position embedding in place, rotate-half form: kernel.attn.rope
+ * (dialect.cpp:40). Rows are tokens b*L + pos (row stride ld elements); heads
+ * are consecutive head_dim-wide column blocks; for i < head_dim/2,
+ * theta = pos * base^(-2i/head_dim), (x[i], x[i+hd/2]) rotated by theta.
+ * base <= 0 selects 10000. */
+int kvm_sm100_rope_bf16(void* x, int64_t ld, int rows, int L, int heads,
+                        int head_dim, float base, kvm_stream_t stream);
+
 /* ------------------------------------------------ graph execution helpers --- */
 
 /* Element types of the elementwise interpreter and kvm_sm100_moe_topk. */

@@ -77,6 +77,10 @@ SIGNATURES = {
     "kvm_sm100_quantize_e4m3_block128": (_I, [_P, _I, _P, _P, _I, _I, _P]),
     "kvm_sm100_transpose_u8": (_I, [_P, _P, _I, _I, _P]),
     "kvm_sm100_transpose_f32": (_I, [_P, _P, _I, _I, _P]),
+    "kvm_sm100_attention_workspace": (_I64, [_I, _I, _I, _I]),
+    "kvm_sm100_attention_prefill_bf16": (_I, [_P, _I64, _P, _I64, _P, _I64, _P, _I64, _I, _I,
+                                              _I, _I, _I, _F, _P, _I64, _P]),
+    "kvm_sm100_rope_bf16": (_I, [_P, _I64, _I, _I, _I, _I, _F, _P]),
     "kvm_sm100_elementwise": (_I, [_P, _P, _P, _I64, _P]),
     "kvm_sm100_gemv_bf16": (_I, [_P, _I64, _P, _P, _I, _I, _I, _P]),
     "kvm_sm100_moe_topk": (_I, [_P, _I, _I, _I, _I, _P, _P, _P]),

@@ -207,6 +207,38 @@ def matmul_fp8(aq: torch.Tensor, sa: torch.Tensor, wq: torch.Tensor, sw: torch.T
     return out
 
 
+# -------------------------------------------------------------- attention ---
+
+def attention_prefill(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, batch: int,
+                      heads_q: int, heads_kv: int, scale: float = 0.0,
+                      out: torch.Tensor | None = None,
+                      workspace: torch.Tensor | None = None) -> torch.Tensor:
+    """Causal GQA attention; q [B*L, HQ*128], k/v [B*L, HKV*128] (row views ok)."""
+    for t, n in ((q, "q"), (k, "k"), (v, "v")):
+        _check(t, n, torch.bfloat16, 2)
+    rows = q.shape[0]
+    L = rows // batch
+    if out is None:
+        out = torch.empty((rows, heads_q * 128), dtype=torch.bfloat16, device=q.device)
+    need = int(_lib.lib().kvm_sm100_attention_workspace(batch, L, heads_q, heads_kv))
+    if workspace is None or workspace.numel() < need:
+        workspace = torch.empty(need, dtype=torch.uint8, device=q.device)
+    call("kvm_sm100_attention_prefill_bf16", q.data_ptr(), _rowmajor(q, "q"), k.data_ptr(),
+         _rowmajor(k, "k"), v.data_ptr(), _rowmajor(v, "v"), out.data_ptr(),
+         _rowmajor(out, "out"), batch, L, heads_q, heads_kv, 128, float(scale),
+         workspace.data_ptr(), workspace.numel(), _stream())
+    return out
+
+
+def rope_(x: torch.Tensor, *, seq_len: int, heads: int, head_dim: int = 128,
+          base: float = 10000.0) -> torch.Tensor:
+    """In-place rotary embedding of x [B*L, >= heads*head_dim] (a row view is ok)."""
+    _check(x, "x", torch.bfloat16, 2)
+    call("kvm_sm100_rope_bf16", x.data_ptr(), _rowmajor(x, "x"), x.shape[0], seq_len, heads,
+         head_dim, float(base), _stream())
+    return x
+
+
 # ------------------------------------------------------------ elementwise ---
 
 def rmsnorm(x: torch.Tensor, gamma: torch.Tensor | None = None, eps: float = 1e-5,
@@ -353,7 +385,7 @@ def device_status() -> int:
 
 __all__ = [
     "matmul", "gemm", "pack_gate_up", "quantize_e4m3", "matmul_fp8", "transpose_u8",
-    "transpose_f32", "transpose", "silu_gate_matmul", "rmsnorm",
+    "transpose_f32", "attention_prefill", "rope_", "transpose", "silu_gate_matmul", "rmsnorm",
     "silu_mul", "moe_route", "moe_permute", "moe_scatter_rows", "grouped_matmul",
     "moe_combine", "Routing", "Dispatch", "device_status", "KVM_B_KN", "KVM_B_NK",
 ]

@@ -60,6 +60,8 @@ def lib() -> C.CDLL:
         L.orc_e4m3_to_f32.argtypes = [C.c_uint8]
         L.orc_quantize_e4m3_block128.argtypes = [P, I, I, P, P]
         L.orc_gemm_fp8_blockscaled.argtypes = [P, P, P, P, P, I, I, I]
+        L.orc_rope_bf16.argtypes = [P, I64, I, I, I, I, F]
+        L.orc_attention_bf16.argtypes = [P, I64, P, I64, P, I64, P, I64, I, I, I, I, I, F]
         _lib = L
     return _lib
 
@@ -242,6 +244,24 @@ def gemm_fp8_blockscaled(aq, sa, wq, sw) -> np.ndarray:
     N = wq.shape[0]
     out = np.empty((M, N), dtype=np.uint16)
     lib().orc_gemm_fp8_blockscaled(_p(aq), _p(sa), _p(wq), _p(sw), _p(out), M, N, K)
+    return out
+
+
+def rope(x: np.ndarray, L: int, heads: int, hd: int = 128, base: float = 10000.0):
+    """Rotary embedding of a [rows, heads*hd] bf16 matrix (returns a copy)."""
+    x = np.array(_c(x, np.uint16), copy=True)
+    lib().orc_rope_bf16(_p(x), x.shape[1], x.shape[0], L, heads, hd, base)
+    return x
+
+
+def attention(q, k, v, B: int, HQ: int, HKV: int, hd: int = 128, scale: float = 0.0):
+    q, k, v = _c(q, np.uint16), _c(k, np.uint16), _c(v, np.uint16)
+    L = q.shape[0] // B
+    if scale <= 0:
+        scale = 1.0 / np.sqrt(hd)
+    out = np.empty((q.shape[0], HQ * hd), dtype=np.uint16)
+    lib().orc_attention_bf16(_p(q), q.shape[1], _p(k), k.shape[1], _p(v), v.shape[1],
+                             _p(out), out.shape[1], B, L, HQ, HKV, hd, float(scale))
     return out
 
 

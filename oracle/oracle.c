@@ -450,3 +450,71 @@ void orc_gemm_fp8_blockscaled(const uint8_t* Aq, const float* sA,
     }
   }
 }
+
+/* ------------------------------------------------------------ attention */
+
+/* Rotary embedding in place, rotate-half form: rows are tokens b*L + pos,
+ * heads are hd-wide column blocks; theta = pos * base^(-2i/hd), i < hd/2. */
+void orc_rope_bf16(uint16_t* x, int64_t ld, int rows, int L, int heads, int hd,
+                   float base) {
+  const int half = hd / 2;
+#pragma omp parallel for schedule(static)
+  for (int r = 0; r < rows; ++r) {
+    const int pos = r % L;
+    for (int h = 0; h < heads; ++h) {
+      uint16_t* v = x + (int64_t)r * ld + (int64_t)h * hd;
+      for (int j = 0; j < half; ++j) {
+        const float inv_freq = powf(base, -2.0f * (float)j / (float)hd);
+        const float ang = (float)pos * inv_freq;
+        const float sn = sinf(ang), cs = cosf(ang);
+        const float a = bf2f(v[j]), b = bf2f(v[j + half]);
+        v[j] = f2bf(a * cs - b * sn);
+        v[j + half] = f2bf(b * cs + a * sn);
+      }
+    }
+  }
+}
+
+/* Causal GQA attention (see kvm_sm100_attention_prefill_bf16): per (b, h),
+ * s[c] = dot(q, k_c) (16-lane order) for keys c <= pos, m = max(scale*s),
+ * l = sum_c exp(scale*s[c] - m) (index order), p_c = bf16(exp(scale*s[c] - m) *
+ * (1/l)), out = bf16(sum_c p_c v_c) (16-lane order over c). */
+void orc_attention_bf16(const uint16_t* q, int64_t ldq, const uint16_t* k,
+                        int64_t ldk, const uint16_t* v, int64_t ldv, uint16_t* out,
+                        int64_t ldo, int B, int L, int HQ, int HKV, int hd,
+                        float scale) {
+  const int group = HQ / HKV;
+#pragma omp parallel for collapse(2) schedule(dynamic, 1)
+  for (int b = 0; b < B; ++b)
+    for (int h = 0; h < HQ; ++h) {
+      const int kh = h / group;
+      float* qf = (float*)malloc(sizeof(float) * (size_t)hd);
+      float* s = (float*)malloc(sizeof(float) * (size_t)L);
+      float* pf = (float*)malloc(sizeof(float) * (size_t)L);
+      for (int pos = 0; pos < L; ++pos) {
+        const int64_t qr = (int64_t)(b * L + pos);
+        for (int d = 0; d < hd; ++d) qf[d] = bf2f(q[qr * ldq + (int64_t)h * hd + d]);
+        float m = -INFINITY;
+        for (int c = 0; c <= pos; ++c) {
+          const uint16_t* kr = k + (int64_t)(b * L + c) * ldk + (int64_t)kh * hd;
+          s[c] = dot_f32_bf16(qf, kr, hd);
+          m = fmaxf(m, s[c] * scale);
+        }
+        float l = 0.0f;
+        for (int c = 0; c <= pos; ++c) l += expf(s[c] * scale - m);
+        const float inv = 1.0f / l;
+        for (int c = 0; c <= pos; ++c) pf[c] = bf2f(f2bf(expf(s[c] * scale - m) * inv));
+        for (int d = 0; d < hd; ++d) {
+          float lanes[LANES] = {0};
+          for (int c = 0; c <= pos; ++c) {
+            const float vv = bf2f(v[(int64_t)(b * L + c) * ldv + (int64_t)kh * hd + d]);
+            lanes[c % LANES] = lanes[c % LANES] + pf[c] * vv;
+          }
+          out[qr * ldo + (int64_t)h * hd + d] = f2bf(lanes_sum(lanes));
+        }
+      }
+      free(qf);
+      free(s);
+      free(pf);
+    }
+}

@@ -138,3 +138,44 @@ def test_moe_layer_composes_the_steps():
     h = oracle.grouped_gemm(xp, w13, off, silu_gate=True)
     y = oracle.grouped_gemm(h, w2, off)
     assert np.array_equal(out, oracle.moe_combine(y, pos, tw))
+
+
+def test_attention_oracle_matches_float64():
+    rng = np.random.default_rng(8)
+    B, L, HQ, HKV, hd = 2, 40, 4, 2, 128
+    q = oracle.normal_bf16(rng, (B * L, HQ * hd))
+    k = oracle.normal_bf16(rng, (B * L, HKV * hd))
+    v = oracle.normal_bf16(rng, (B * L, HKV * hd))
+    out = oracle.bf16_to_f32(oracle.attention(q, k, v, B, HQ, HKV))
+    qf, kf, vf = (oracle.bf16_to_f32(a).astype(np.float64) for a in (q, k, v))
+    ref = np.zeros_like(out, dtype=np.float64)
+    for b in range(B):
+        for h in range(HQ):
+            kh = h // (HQ // HKV)
+            Q = qf[b * L:(b + 1) * L, h * hd:(h + 1) * hd]
+            K = kf[b * L:(b + 1) * L, kh * hd:(kh + 1) * hd]
+            V = vf[b * L:(b + 1) * L, kh * hd:(kh + 1) * hd]
+            S = Q @ K.T / np.sqrt(hd)
+            S[np.triu_indices(L, 1)] = -np.inf
+            P = np.exp(S - S.max(1, keepdims=True))
+            P /= P.sum(1, keepdims=True)
+            ref[b * L:(b + 1) * L, h * hd:(h + 1) * hd] = P @ V
+    assert rel_err(out, ref) < 1e-2
+
+
+def test_rope_oracle_matches_float64():
+    rng = np.random.default_rng(9)
+    L, heads, hd = 16, 2, 128
+    x = oracle.normal_bf16(rng, (2 * L, heads * hd))
+    got = oracle.bf16_to_f32(oracle.rope(x, L, heads))
+    xf = oracle.bf16_to_f32(x).astype(np.float64)
+    ref = np.empty_like(xf)
+    for r in range(2 * L):
+        pos = r % L
+        for h in range(heads):
+            v = xf[r, h * hd:(h + 1) * hd]
+            th = pos * 10000.0 ** (-2.0 * np.arange(hd // 2) / hd)
+            a, b = v[:hd // 2], v[hd // 2:]
+            ref[r, h * hd:h * hd + hd // 2] = a * np.cos(th) - b * np.sin(th)
+            ref[r, h * hd + hd // 2:(h + 1) * hd] = b * np.cos(th) + a * np.sin(th)
+    assert rel_err(got, ref) < 4e-3
