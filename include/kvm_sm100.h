@@ -238,12 +238,20 @@ int kvm_sm100_ep_combine(const kvm_ep_peers* peers, const int32_t* topk_idx,
  * Wq: e4m3 [N, K] (K contiguous; weights in kernel.matmul's [K, N] layout are
  * converted once with kvm_sm100_transpose_u8 / kvm_sm100_transpose_f32);
  * sW: fp32 [N/128, K/128]. K % 128 == 0, N % 128 == 0.
+ * When M is small (one or two 128-row tiles) the K blocks of each tile are
+ * split over several work units so that every SM streams weights; each unit
+ * then accumulates its own blocks and the units' fp32 partials are summed in
+ * unit order. That needs kvm_sm100_gemm_fp8_workspace(M, N, K) bytes of
+ * workspace (0 = no split; with a NULL or smaller workspace the GEMM runs
+ * unsplit).
  * The reference cannot express this op (src/ir/dialect/dtype.h:13-20 has no
  * fp8); it is the sm_100a form of task.tc.mma_acc (task/dialect.cpp:34) on
  * e4m3 operands. */
+int64_t kvm_sm100_gemm_fp8_workspace(int M, int N, int K);
 int kvm_sm100_gemm_fp8_blockscaled(const void* Aq, const float* sA,
                                    const void* Wq, const float* sW, void* D,
                                    int64_t ldd, int M, int N, int K,
+                                   void* workspace, int64_t workspace_bytes,
                                    kvm_stream_t stream);
 
 /* Quantise x [R, C] (x_dtype KVM_BF16 or KVM_F32) to e4m3 per 128x128 block:

@@ -73,7 +73,9 @@ SIGNATURES = {
     "kvm_sm100_ep_wait": (_I, [_P, _I, C.c_uint32, _P]),
     "kvm_sm100_ep_signal": (_I, [_P, _I, C.c_uint32, _P]),
     "kvm_sm100_ep_combine": (_I, [_P, _P, _P, _P, _P, _P, _P, _I, _I64, _P]),
-    "kvm_sm100_gemm_fp8_blockscaled": (_I, [_P, _P, _P, _P, _P, _I64, _I, _I, _I, _P]),
+    "kvm_sm100_gemm_fp8_workspace": (_I64, [_I, _I, _I]),
+    "kvm_sm100_gemm_fp8_blockscaled": (_I, [_P, _P, _P, _P, _P, _I64, _I, _I, _I, _P, _I64,
+                                            _P]),
     "kvm_sm100_quantize_e4m3_block128": (_I, [_P, _I, _P, _P, _I, _I, _P]),
     "kvm_sm100_transpose_u8": (_I, [_P, _P, _I, _I, _P]),
     "kvm_sm100_transpose_f32": (_I, [_P, _P, _I, _I, _P]),

@@ -60,7 +60,103 @@ def _line(args, clocks, t0, t1, **kw):
     print(json.dumps(base), flush=True)
 
 
+def run_tp(args, peaks, ClockSampler) -> int:
+    """Tensor-parallel decoder layer: hidden 8192, 64 query / 8 kv heads of 128,
+    batch 4 x seq 2048, FFN 28672; P ranks (torchrun), strong scaling."""
+    import os
+    import torch.distributed as dist
+    from datetime import timedelta
+    from .tp import TPDecoderLayer
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    B, L, H, HQ, HKV, FF = 4, 2048, 8192, 64, 8, 28672
+    hq, hkv, fr = HQ // world, HKV // world, FF // world
+    g = torch.Generator(device=dev)
+    g.manual_seed(100 + rank)
+
+    def rnd(*shape, std=0.02):
+        return (torch.randn(shape, generator=g, device=dev) * std).to(torch.bfloat16)
+    wqkv = rnd((hq + 2 * hkv) * 128, H)
+    wo = rnd(H, hq * 128)
+    w13 = torch.empty((2 * fr, H), dtype=torch.bfloat16, device=dev)
+    for i in range(0, 2 * fr, 4096):
+        w13[i:i + 4096] = rnd(min(4096, 2 * fr - i), H)
+    w2 = rnd(H, fr)
+    ones = torch.ones(H, dtype=torch.bfloat16, device=dev)
+    g.manual_seed(7)
+    x = torch.randn((B * L, H), generator=g, device=dev).to(torch.bfloat16)
+    layer = TPDecoderLayer(wqkv, wo, w13, w2, ones, ones, batch=B, seq_len=L, heads_q=HQ,
+                           heads_kv=HKV, rank=rank, world=world)
+    steps, warmup = args.steps, max(args.warmup, 3)
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(steps)]
+    for _ in range(warmup):
+        layer(x)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier(device_ids=[local])
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as ck:
+        t0 = time.time()
+        e0.record()
+        for i in range(steps):
+            layer(x, probe=ev[i])
+        e1.record()
+        torch.cuda.synchronize()
+        t1 = time.time()
+    ms = e0.elapsed_time(e1) / steps
+    att_ms = statistics.mean(a.elapsed_time(b) for a, b in ev)
+    ar_ms = None
+    if world > 1:
+        buf = torch.randn((B * L, H), device=dev).to(torch.bfloat16)
+        for _ in range(3):
+            dist.all_reduce(buf)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(10):
+            dist.all_reduce(buf)
+        b.record()
+        torch.cuda.synchronize()
+        ar_ms = a.elapsed_time(b) / 10
+        t = torch.tensor([ms, att_ms, ar_ms], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms, att_ms, ar_ms = (float(v) for v in t)
+    T = B * L
+    flop_lin = 2.0 * T * H * ((HQ + 2 * HKV) * 128 + HQ * 128 + 3 * FF)
+    flop_att = 2.0 * 2.0 * B * HQ * L * L * 128 / 2
+    tf = (flop_lin + flop_att) / (ms / 1e3) / 1e12
+    att_tf = flop_att / world / (att_ms / 1e3) / 1e12
+    if rank == 0:
+        ar = None
+        if ar_ms:
+            nbytes = T * H * 2
+            ar = {"ms": ar_ms, "algbw_gbs": nbytes / (ar_ms / 1e3) / 1e9,
+                  "busbw_gbs": nbytes * 2 * (world - 1) / world / (ar_ms / 1e3) / 1e9}
+        _line(args, ck, t0, t1, metric="TP decoder layer tokens/s", value=T / (ms / 1e3),
+              unit="tokens/s", ms_per_step=ms, n_gpus=world, scaling="strong", dtype="bf16",
+              config={"workload": "tp_decoder_H8192_HQ64_HKV8_B4_L2048_F28672",
+                      "parallelism": f"tp{world}", "tflops_total": tf,
+                      "tflops_per_gpu": tf / world, "attention_ms": att_ms,
+                      "attention_tflops_per_gpu": att_tf, "allreduce_8192x8192_bf16": ar},
+              roofline={"bound": "tensor", "achieved": tf / world,
+                        "peak": peaks["bf16_sustained"], "unit": "TFLOP/s",
+                        "frac": tf / world / peaks["bf16_sustained"], "traffic": None,
+                        "kernel": "whole layer (GEMMs dominate)"},
+              gpu_launches=layer.launches() * steps)
+    if world > 1:
+        dist.barrier(device_ids=[local])
+        dist.destroy_process_group()
+    return 0
+
+
 def run(args, peaks, ClockSampler) -> int:
+    if args.workload == "tp":
+        return run_tp(args, peaks, ClockSampler)
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
     g = torch.Generator(device=dev)
@@ -132,7 +228,11 @@ def run(args, peaks, ClockSampler) -> int:
             a = torch.randn((M, K), generator=g, device=dev)
             aq, sa = ops.quantize_e4m3(a)
             d = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
-            ms = _time(lambda: ops.matmul_fp8(aq, sa, wq, sw, out=d), steps, warmup)
+            from ._lib import lib
+            wsz = int(lib().kvm_sm100_gemm_fp8_workspace(M, N, K))
+            ws = torch.empty(max(wsz, 16), dtype=torch.uint8, device=dev)
+            ms = _time(lambda: ops.matmul_fp8(aq, sa, wq, sw, out=d, workspace=ws), steps,
+                       warmup)
             flop = 2.0 * M * N * K
             byt = M * K + K * N + 4 * (sa.numel() + sw.numel()) + 2 * M * N
             res[M] = {"ms": ms, "tflops": flop / (ms / 1e3) / 1e12,

@@ -30,6 +30,8 @@ struct Fp8Params {
   __nv_bfloat16* D;
   long long ldd;
   int* status;
+  int splits;        // > 1: the K blocks of each tile are split over `splits`
+  float* partial;    //      work units; each writes an fp32 partial tile here
 };
 
 template <int BN, int STAGES, int NBUF>
@@ -71,8 +73,17 @@ __global__ void __launch_bounds__(kF8Threads, 1)
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int m_tiles = (p.M + kF8BM - 1) / kF8BM;
   const int n_tiles = p.N / BN;
-  const int total = m_tiles * n_tiles;
+  const int splits = p.splits > 1 ? p.splits : 1;
+  const int total = m_tiles * n_tiles * splits;
   const int kbs = p.K / kF8BK;
+  // unit t: tile t / splits (N-tile major), K blocks [kb0, kb1) of split t % splits
+  auto unit = [&](int t, int& nt, int& mt, int& kb0, int& kb1) {
+    const int tile = t / splits, sp = t - tile * splits;
+    nt = tile / m_tiles;
+    mt = tile - nt * m_tiles;
+    kb0 = static_cast<int>(static_cast<long long>(sp) * kbs / splits);
+    kb1 = static_cast<int>(static_cast<long long>(sp + 1) * kbs / splits);
+  };
 
   if (threadIdx.x == 0) {
     *abort_flag = 0;
@@ -106,8 +117,9 @@ __global__ void __launch_bounds__(kF8Threads, 1)
       uint32_t ph = 0;
       bool ok = true;
       for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
-        const int nt = t / m_tiles, mt = t - nt * m_tiles;
-        for (int kb = 0; kb < kbs; ++kb) {
+        int nt, mt, kb0, kb1;
+        unit(t, nt, mt, kb0, kb1);
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&empty[s], ph ^ 1, abort_flag)) { ok = false; break; }
           uint8_t* a_dst = smem + s * S::kStage;
           mbar_arrive_expect_tx(&full[s], S::kStage);
@@ -132,7 +144,9 @@ __global__ void __launch_bounds__(kF8Threads, 1)
       uint32_t g = 0;  // K blocks issued so far (selects the TMEM buffer)
       bool ok = true;
       for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
-        for (int kb = 0; kb < kbs; ++kb, ++g) {
+        int nt, mt, kb0, kb1;
+        unit(t, nt, mt, kb0, kb1);
+        for (int kb = kb0; kb < kb1; ++kb, ++g) {
           const uint32_t b = g % NBUF, bph = (g / NBUF) & 1;
           if (!mbar_wait(&tempty[b], bph ^ 1, abort_flag)) { ok = false; break; }
           if (!mbar_wait(&full[s], ph, abort_flag)) { ok = false; break; }
@@ -161,14 +175,15 @@ __global__ void __launch_bounds__(kF8Threads, 1)
     uint32_t g = 0;
     bool ok = true;
     for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
-      const int nt = t / m_tiles, mt = t - nt * m_tiles;
+      int nt, mt, kb0, kb1;
+      unit(t, nt, mt, kb0, kb1);
       const int row = mt * kF8BM + r_in;
       float acc[HALF];
 #pragma unroll
       for (int j = 0; j < HALF; ++j) acc[j] = 0.f;
       const float* sa = p.sA + static_cast<long long>(mt) * kbs;
       const float* sw = p.sW + static_cast<long long>(nt) * kbs;
-      for (int kb = 0; kb < kbs; ++kb, ++g) {
+      for (int kb = kb0; kb < kb1; ++kb, ++g) {
         const uint32_t b = g % NBUF, bph = (g / NBUF) & 1;
         const bool ready = mbar_wait(&tfull[b], bph, abort_flag);
         if (!__all_sync(0xffffffffu, ready)) { ok = false; break; }
@@ -189,7 +204,15 @@ __global__ void __launch_bounds__(kF8Threads, 1)
           acc[j] = __fmaf_rn(__uint_as_float(v[j]), sc, acc[j]);
       }
       if (!ok) break;
-      if (row < p.M) {
+      if (splits > 1) {
+        if (row < p.M) {  // fp32 partial [unit][128 rows][BN], valid rows only
+          float4* dst = reinterpret_cast<float4*>(
+              p.partial + (static_cast<long long>(t) * kF8BM + r_in) * BN + h * HALF);
+#pragma unroll
+          for (int i = 0; i < HALF / 4; ++i)
+            dst[i] = make_float4(acc[4 * i], acc[4 * i + 1], acc[4 * i + 2], acc[4 * i + 3]);
+        }
+      } else if (row < p.M) {
         uint4* dst = reinterpret_cast<uint4*>(
             p.D + static_cast<long long>(row) * p.ldd + nt * BN + h * HALF);
 #pragma unroll
@@ -209,6 +232,47 @@ __global__ void __launch_bounds__(kF8Threads, 1)
     tc_fence_after();
     tmem_dealloc(tmem_base, S::kTmemCols);
   }
+}
+
+// Sum of the split partials in split order, to bf16: one thread per 8 outputs.
+__global__ void fp8_split_reduce_kernel(const float* __restrict__ partial,
+                                        __nv_bfloat16* __restrict__ D, long long ldd,
+                                        int M, int N, int m_tiles, int splits, int BN) {
+  const long long i = (blockIdx.x * 256ll + threadIdx.x) * 8;
+  if (i >= static_cast<long long>(M) * N) return;
+  const int row = static_cast<int>(i / N), col = static_cast<int>(i % N);
+  const int nt = col / BN, mt = row / kF8BM;
+  const long long tile = static_cast<long long>(nt) * m_tiles + mt;
+  float a[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  for (int sp = 0; sp < splits; ++sp) {
+    const float* src = partial + ((tile * splits + sp) * kF8BM + row % kF8BM) * BN + col % BN;
+    const float4 x = reinterpret_cast<const float4*>(src)[0];
+    const float4 y = reinterpret_cast<const float4*>(src)[1];
+    a[0] += x.x; a[1] += x.y; a[2] += x.z; a[3] += x.w;
+    a[4] += y.x; a[5] += y.y; a[6] += y.z; a[7] += y.w;
+  }
+  *reinterpret_cast<uint4*>(D + static_cast<long long>(row) * ldd + col) =
+      make_uint4(pack_bf16x2(a[0], a[1]), pack_bf16x2(a[2], a[3]),
+                 pack_bf16x2(a[4], a[5]), pack_bf16x2(a[6], a[7]));
+}
+
+// K splits so that every SM gets a work unit when there are fewer output
+// tiles than SMs; with at least one tile per SM the partial traffic costs more
+// than the balance gains (measured at M = 16 and 128 with N = 28672).
+int choose_splits(int tiles, int kbs, int sms) {
+  if (tiles >= sms) return 1;
+  int best = 1;
+  double best_eff = 0.0;
+  for (int s = 1; s <= 8 && kbs / s >= 4; ++s) {
+    const long long units = static_cast<long long>(tiles) * s;
+    const long long waves = (units + sms - 1) / sms;
+    const double eff = static_cast<double>(units) / (waves * sms);
+    if (eff > best_eff + 0.02) {
+      best_eff = eff;
+      best = s;
+    }
+  }
+  return best;
 }
 
 // 128x128 block quantiser: one block of 256 threads per 128x128 tile.
@@ -292,10 +356,20 @@ __global__ void transpose_f32_kernel(const float* __restrict__ in,
 
 using namespace kvm;
 
+extern "C" int64_t kvm_sm100_gemm_fp8_workspace(int M, int N, int K) {
+  if (M <= 0 || N <= 0 || K <= 0 || K % 128 != 0 || N % 128 != 0) return 0;
+  const DeviceInfo* dev = device_info();
+  const int sms = dev ? dev->sm_count : 148;
+  const int tiles = ((M + kF8BM - 1) / kF8BM) * (N / 128);
+  const int splits = choose_splits(tiles, K / kF8BK, sms);
+  return splits > 1 ? static_cast<int64_t>(tiles) * splits * kF8BM * 128 * 4 : 0;
+}
+
 extern "C" int kvm_sm100_gemm_fp8_blockscaled(const void* Aq, const float* sA,
                                               const void* Wq, const float* sW,
                                               void* D, int64_t ldd, int M,
-                                              int N, int K,
+                                              int N, int K, void* workspace,
+                                              int64_t workspace_bytes,
                                               kvm_stream_t stream) {
   constexpr int BN = 128, STAGES = 6, NBUF = 4;
   if (M <= 0 || N <= 0 || K <= 0 || K % 128 != 0 || N % BN != 0)
@@ -311,15 +385,30 @@ extern "C" int kvm_sm100_gemm_fp8_blockscaled(const void* Aq, const float* sA,
                          CU_TENSOR_MAP_DATA_TYPE_UINT8, CU_TENSOR_MAP_SWIZZLE_128B));
   KVM_TRY(encode_tmap_2d(&tb, Wq, K, N, K, kF8BK, BN,
                          CU_TENSOR_MAP_DATA_TYPE_UINT8, CU_TENSOR_MAP_SWIZZLE_128B));
-  Fp8Params p{M, N, K, sA, sW, static_cast<__nv_bfloat16*>(D), ldd, dev->status};
-  const int tiles = ((M + kF8BM - 1) / kF8BM) * (N / BN);
-  const int grid = tiles < dev->sm_count ? tiles : dev->sm_count;
+  const int m_tiles = (M + kF8BM - 1) / kF8BM;
+  const int tiles = m_tiles * (N / BN);
+  int splits = choose_splits(tiles, K / kF8BK, dev->sm_count);
+  const int64_t need = static_cast<int64_t>(tiles) * splits * kF8BM * BN * 4;
+  if (splits > 1 && (!workspace || workspace_bytes < need || !aligned16(workspace)))
+    splits = 1;  // no room for partials: one unit per tile
+  Fp8Params p{M, N, K, sA, sW, static_cast<__nv_bfloat16*>(D), ldd, dev->status,
+              splits, static_cast<float*>(workspace)};
+  const int units = tiles * splits;
+  const int grid = units < dev->sm_count ? units : dev->sm_count;
   auto kern = gemm_fp8_bs_kernel<BN, STAGES, NBUF>;
   constexpr size_t smem = Fp8Smem<BN, STAGES, NBUF>::kTotal;
   KVM_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     int(smem)));
   kern<<<grid, kF8Threads, smem, static_cast<cudaStream_t>(stream)>>>(ta, tb, p);
   KVM_CUDA_TRY(cudaGetLastError());
+  if (splits > 1) {
+    const long long n8 = (static_cast<long long>(M) * N) / 8;
+    fp8_split_reduce_kernel<<<static_cast<unsigned>((n8 + 255) / 256), 256, 0,
+                              static_cast<cudaStream_t>(stream)>>>(
+        static_cast<const float*>(workspace), static_cast<__nv_bfloat16*>(D), ldd, M, N,
+        m_tiles, splits, BN);
+    KVM_CUDA_TRY(cudaGetLastError());
+  }
   return KVM_OK;
 }
 

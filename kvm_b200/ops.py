@@ -182,7 +182,8 @@ def transpose_f32(x: torch.Tensor) -> torch.Tensor:
 
 
 def matmul_fp8(aq: torch.Tensor, sa: torch.Tensor, wq: torch.Tensor, sw: torch.Tensor,
-               out: torch.Tensor | None = None) -> torch.Tensor:
+               out: torch.Tensor | None = None,
+               workspace: torch.Tensor | None = None) -> torch.Tensor:
     """D = sum_kb sA*sW * (Aq . Wq^T) over 128-deep blocks, bf16 out.
 
     aq: uint8 e4m3 [M, K]; sa fp32 [ceil(M/128), K/128]; wq: uint8 e4m3 [N, K];
@@ -202,8 +203,12 @@ def matmul_fp8(aq: torch.Tensor, sa: torch.Tensor, wq: torch.Tensor, sw: torch.T
             raise ValueError(f"{n} must be contiguous")
     if out is None:
         out = torch.empty((M, N), dtype=torch.bfloat16, device=aq.device)
+    need = int(_lib.lib().kvm_sm100_gemm_fp8_workspace(M, N, K))
+    if need and (workspace is None or workspace.numel() < need):
+        workspace = torch.empty(need, dtype=torch.uint8, device=aq.device)
     call("kvm_sm100_gemm_fp8_blockscaled", aq.data_ptr(), sa.data_ptr(), wq.data_ptr(),
-         sw.data_ptr(), out.data_ptr(), _rowmajor(out, "out"), M, N, K, _stream())
+         sw.data_ptr(), out.data_ptr(), _rowmajor(out, "out"), M, N, K,
+         _ptr(workspace) if need else None, need, _stream())
     return out
 
 
