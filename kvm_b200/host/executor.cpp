@@ -2,6 +2,8 @@
 #include "executor.h"
 
 #include <any>
+#include <cmath>
+#include <cstdlib>
 #include <cstring>
 #include <stdexcept>
 #include <string>
@@ -105,11 +107,31 @@ struct Executor::Routing {
 
 struct Executor::Slot {
   enum Kind { kGlobal, kView, kMma, kExpr } kind = kGlobal;
-  Buffer buf;                             // kGlobal
+  Buffer buf;                             // kGlobal (ptr null until planned)
   const ir::ValueNode* base = nullptr;    // kView: the viewed global value
   std::vector<const ir::ValueNode*> args; // kMma (a, b[, c]) / kExpr operands
   std::string op;                         // kExpr: "alu.add", "sfu.exp", ...
   Routing* group = nullptr;               // rows grouped by a moe_dispatch
+};
+
+// Semantic view of an expression for pattern matching: loads and inlined
+// globals are looked through, a * rcp(b) reads as div(a, b).
+struct Executor::SNode {
+  std::string op;                        // "" for a leaf
+  std::vector<SNode> args;
+  const ir::ValueNode* leaf = nullptr;   // the global a leaf reads
+  bool is(const char* o) const { return op == o; }
+};
+
+struct Executor::SiluMatch {
+  const ir::ValueNode* g = nullptr;  // gate GEMM result (not materialised)
+  const ir::ValueNode* u = nullptr;  // up GEMM result (not materialised)
+};
+
+struct Executor::RmsMatch {
+  const ir::ValueNode* x = nullptr;
+  const ir::ValueNode* gamma = nullptr;  // may be null
+  float eps = 0.f;
 };
 
 Executor::Executor(const ir::Graph& kernel, const ir::AttrMap& attrs)
@@ -143,24 +165,22 @@ Executor::Slot& Executor::slot(const ir::ValueNode* v) {
   return *it->second;
 }
 
+const ir::ValueNode* Executor::BaseGlobal(const ir::ValueNode* v) {
+  while (slot(v).kind == Slot::kView) v = slot(v).base;
+  return v;
+}
+
 const Buffer& Executor::GlobalOf(const ir::ValueNode* v) {
-  Slot* s = &slot(v);
-  while (s->kind == Slot::kView) s = &slot(s->base);
-  if (s->kind != Slot::kGlobal)
+  Slot& s = slot(BaseGlobal(v));
+  if (s.kind != Slot::kGlobal || !s.buf.ptr)
     Fail("value %" + v->value().name + " is read before it is stored");
-  return s->buf;
+  return s.buf;
 }
 
 Buffer& Executor::Materialize(const ir::ValueNode* v) {
-  const auto& t = TaskTensorOf(v);
-  auto s = std::make_unique<Slot>();
-  s->kind = Slot::kGlobal;
-  s->buf.shape.assign(t.shape.begin(), t.shape.end());
-  s->buf.dtype = t.dtype;
-  s->buf.ptr = Alloc(s->buf.bytes());
-  Buffer& b = s->buf;
-  slots_[v] = std::move(s);
-  return b;
+  Slot& s = slot(v);
+  if (!s.buf.ptr) s.buf.ptr = Alloc(s.buf.bytes());
+  return s.buf;
 }
 
 const ir::OpNode* Executor::KernelCommOp(const std::string& name, int nth) const {
@@ -170,25 +190,48 @@ const ir::OpNode* Executor::KernelCommOp(const std::string& name, int nth) const
   return nullptr;
 }
 
-void Executor::Prepare() {
-  if (prepared_) return;
+bool Executor::InputFill(const ir::ValueNode* v, double* value) const {
+  const auto& targs = task_.root()->arguments();
+  for (std::size_t i = 0; i < targs.size(); ++i) {
+    if (targs[i] != v) continue;
+    const std::any* a = attrs_.Get(kernel_.root()->arguments()[i], "fill");
+    if (!a) return false;
+    if (const auto* d = std::any_cast<double>(a)) { *value = *d; return true; }
+    if (const auto* n = std::any_cast<std::int64_t>(a)) { *value = double(*n); return true; }
+    return false;
+  }
+  return false;
+}
+
+void Executor::Analyze() {
   const ir::Block* root = task_.root();
   for (std::size_t i = 0; i < root->arguments().size(); ++i) {
-    inputs_[i].ptr = Alloc(inputs_[i].bytes());
     auto s = std::make_unique<Slot>();
     s->kind = Slot::kGlobal;
     s->buf = inputs_[i];
     slots_[root->arguments()[i]] = std::move(s);
   }
+  auto new_global = [&](const ir::ValueNode* v, Routing* group) {
+    const auto& t = TaskTensorOf(v);
+    auto s = std::make_unique<Slot>();
+    s->kind = Slot::kGlobal;
+    s->buf.shape.assign(t.shape.begin(), t.shape.end());
+    s->buf.dtype = t.dtype;
+    s->group = group;
+    slots_[v] = std::move(s);
+  };
   for (const ir::OpNode* op : root->operations()) {
     const std::string key = OpKey(op);
     const ir::ValueNode* res = op->results().empty() ? nullptr : op->results()[0];
+    for (const ir::ValueNode* a : op->operands()) consumers_[a].push_back(op);
     if (key == "task.tma.gmem_to_smem" || key == "task.lsu.gmem_to_reg" ||
         key == "task.lsu.smem_to_reg") {
+      const ir::ValueNode* g = BaseGlobal(op->operands()[0]);
+      ++uses_[g];
       auto s = std::make_unique<Slot>();
       s->kind = Slot::kView;
       s->base = op->operands()[0];
-      s->group = slot(op->operands()[0]).group;
+      s->group = slot(g).group;
       slots_[res] = std::move(s);
     } else if (key == "task.tc.mma" || key == "task.tc.mma_acc") {
       auto s = std::make_unique<Slot>();
@@ -205,22 +248,314 @@ void Executor::Prepare() {
         if (!s->group) s->group = slot(a).group;
       slots_[res] = std::move(s);
     } else if (key == "task.lsu.reg_to_gmem" || key == "task.tma.smem_to_gmem") {
-      PlanStore(op->operands()[0], res);
+      producer_[res] = op->operands()[0];
+      new_global(res, slot(op->operands()[0]).group);
+      actions_.push_back(op);
     } else if (StartsWith(key, "task.comm.")) {
-      PlanComm(op);
+      for (const ir::ValueNode* a : op->operands()) ++uses_[BaseGlobal(a)];
+      Routing* group = nullptr;
+      if (op->op().op.name == "comm.moe_dispatch") {
+        auto r = std::make_unique<Routing>();
+        group = r.get();
+        routing_by_op_[op] = group;
+        routings_.push_back(std::move(r));
+      }
+      new_global(res, group);
+      actions_.push_back(op);
     } else {
       Fail("no executor rule for task op '" + key + "'");
     }
   }
-  for (const ir::ValueNode* o : root->outputs()) outputs_.push_back(GlobalOf(o));
+  for (const ir::ValueNode* o : root->outputs()) ++uses_[BaseGlobal(o)];
+}
+
+Executor::SNode Executor::Resolve(const ir::ValueNode* v) {
+  Slot& s = slot(v);
+  if (s.kind == Slot::kView) return Resolve(s.base);
+  if (s.kind == Slot::kGlobal) {
+    auto p = producer_.find(v);
+    if (inlined_.count(v) && p != producer_.end()) return Resolve(p->second);
+    SNode n;
+    n.leaf = v;
+    return n;
+  }
+  SNode n;
+  if (s.kind == Slot::kMma) {
+    n.op = "mma";
+    return n;
+  }
+  if (s.op == "alu.mul" && slot(s.args[1]).kind == Slot::kExpr &&
+      slot(s.args[1]).op == "sfu.rcp") {
+    n.op = "div";
+    n.args = {Resolve(s.args[0]), Resolve(slot(s.args[1]).args[0])};
+    return n;
+  }
+  n.op = s.op;
+  for (const ir::ValueNode* a : s.args) n.args.push_back(Resolve(a));
+  return n;
+}
+
+// h = mul(div(g, add(exp(neg(g)), 1)), u) with g, u products of the same A.
+bool Executor::MatchSilu(const ir::ValueNode* dst, SiluMatch* m) {
+  auto pit = producer_.find(dst);
+  if (pit == producer_.end() || slot(pit->second).kind != Slot::kExpr) return false;
+  const SNode h = Resolve(pit->second);
+  if (!h.is("alu.mul") || h.args.size() != 2) return false;
+  for (int side = 0; side < 2; ++side) {
+    const SNode& d = h.args[side];
+    const SNode& u = h.args[1 - side];
+    if (!d.is("div") || !u.leaf) continue;
+    const SNode& x = d.args[0];
+    const SNode& den = d.args[1];
+    if (!x.leaf || !den.is("alu.add")) continue;
+    for (int o = 0; o < 2; ++o) {
+      const SNode& ex = den.args[o];
+      const SNode& one = den.args[1 - o];
+      double fill = 0;
+      if (!ex.is("sfu.exp") || !ex.args[0].is("alu.neg") || !one.leaf) continue;
+      if (ex.args[0].args[0].leaf != x.leaf) continue;
+      if (!InputFill(one.leaf, &fill) || fill != 1.0) continue;
+      const ir::ValueNode* g = x.leaf;
+      const ir::ValueNode* uu = u.leaf;
+      auto pg = producer_.find(g), pu = producer_.find(uu);
+      if (pg == producer_.end() || pu == producer_.end()) return false;
+      Slot& mg = slot(pg->second);
+      Slot& mu = slot(pu->second);
+      if (mg.kind != Slot::kMma || mu.kind != Slot::kMma || mg.args.size() != 2 ||
+          mu.args.size() != 2)
+        return false;
+      if (BaseGlobal(mg.args[0]) != BaseGlobal(mu.args[0])) return false;
+      const Buffer& bg = slot(BaseGlobal(mg.args[1])).buf;
+      const Buffer& bu = slot(BaseGlobal(mu.args[1])).buf;
+      if (bg.shape != bu.shape || bg.dtype != Dtype::kBf16) return false;
+      const int64_t F = bg.shape.back();
+      if (F % 128 != 0 || uses_[g] != 2 || uses_[uu] != 1) return false;
+      if (slot(dst).buf.dtype != Dtype::kBf16) return false;
+      m->g = g;
+      m->u = uu;
+      return true;
+    }
+  }
+  return false;
+}
+
+// y = mul(mul(x, r), gamma) or mul(x, r), r = rsqrt(add(ms, eps)),
+// ms = matmul(sq, invh) with invh = 1/H, sq = mul(x, x).
+bool Executor::MatchRms(const ir::ValueNode* dst, RmsMatch* m) {
+  auto pit = producer_.find(dst);
+  if (pit == producer_.end() || slot(pit->second).kind != Slot::kExpr) return false;
+  SNode y = Resolve(pit->second);
+  const ir::ValueNode* gamma = nullptr;
+  auto find_r = [](const SNode& n, const SNode** x, const SNode** r) {
+    if (!n.is("alu.mul") || n.args.size() != 2) return false;
+    for (int s = 0; s < 2; ++s)
+      if (n.args[s].is("sfu.rsqrt") && n.args[1 - s].leaf) {
+        *x = &n.args[1 - s];
+        *r = &n.args[s];
+        return true;
+      }
+    return false;
+  };
+  const SNode *x = nullptr, *r = nullptr;
+  if (!find_r(y, &x, &r)) {
+    if (!y.is("alu.mul") || y.args.size() != 2) return false;
+    for (int s = 0; s < 2 && !x; ++s)
+      if (y.args[1 - s].leaf && find_r(y.args[s], &x, &r)) gamma = y.args[1 - s].leaf;
+    if (!x) return false;
+  }
+  const SNode& add = r->args[0];
+  if (!add.is("alu.add")) return false;
+  for (int s = 0; s < 2; ++s) {
+    const SNode& ms = add.args[s];
+    const SNode& eps = add.args[1 - s];
+    double ev = 0, inv = 0;
+    if (!ms.leaf || !eps.leaf || !InputFill(eps.leaf, &ev)) continue;
+    auto pm = producer_.find(ms.leaf);
+    if (pm == producer_.end() || slot(pm->second).kind != Slot::kMma) continue;
+    Slot& mm = slot(pm->second);
+    if (mm.args.size() != 2) continue;
+    const ir::ValueNode* sq = BaseGlobal(mm.args[0]);
+    const ir::ValueNode* invh = BaseGlobal(mm.args[1]);
+    const Buffer& xb = slot(x->leaf).buf;
+    if (xb.shape.size() != 2 || xb.dtype != Dtype::kBf16) return false;
+    const int64_t H = xb.shape[1];
+    if (!InputFill(invh, &inv) || std::abs(inv * double(H) - 1.0) > 1e-2) return false;
+    auto ps = producer_.find(sq);
+    if (ps == producer_.end() || slot(ps->second).kind != Slot::kExpr) return false;
+    const SNode sqn = Resolve(ps->second);
+    if (!sqn.is("alu.mul") || sqn.args[0].leaf != x->leaf || sqn.args[1].leaf != x->leaf)
+      return false;
+    if (uses_[sq] != 1 || uses_[ms.leaf] != 1 || H % 8 != 0) return false;
+    if (gamma) {
+      const Buffer& gb = slot(gamma).buf;
+      if (gb.numel() != H || gb.dtype != Dtype::kBf16) return false;
+    }
+    if (slot(dst).buf.dtype != Dtype::kBf16 || slot(dst).buf.numel() != xb.numel())
+      return false;
+    m->x = x->leaf;
+    m->gamma = gamma;
+    m->eps = float(ev);
+    elided_[sq] = true;
+    elided_[ms.leaf] = true;
+    return true;
+  }
+  return false;
+}
+
+void Executor::Fuse() {
+  // KVM_EXEC_NO_FUSION=1 keeps every kernel op a launch of its own.
+  if (const char* e = std::getenv("KVM_EXEC_NO_FUSION"); e && e[0] == '1') return;
+  // 1. inline single-use elementwise results into their one consumer
+  for (const ir::OpNode* op : actions_) {
+    if (StartsWith(OpKey(op), "task.comm.")) continue;
+    const ir::ValueNode* dst = op->results()[0];
+    if (slot(producer_[dst]).kind != Slot::kExpr || uses_[dst] != 1) continue;
+    bool feeds_expr = false;
+    for (const ir::OpNode* c : consumers_[dst]) {
+      if (OpKey(c) != "task.lsu.gmem_to_reg") continue;
+      feeds_expr = true;
+      for (const ir::OpNode* cc : consumers_[c->results()[0]]) {
+        const std::string k = OpKey(cc);
+        if (!StartsWith(k, "task.alu.") && !StartsWith(k, "task.sfu.")) feeds_expr = false;
+      }
+    }
+    if (feeds_expr) inlined_[dst] = true;
+  }
+  // 2. composites
+  for (const ir::OpNode* op : actions_) {
+    if (StartsWith(OpKey(op), "task.comm.")) continue;
+    const ir::ValueNode* dst = op->results()[0];
+    if (inlined_.count(dst)) continue;
+    SiluMatch sm;
+    RmsMatch rm;
+    if (MatchSilu(dst, &sm)) {
+      elided_[sm.g] = elided_[sm.u] = true;
+      silu_[dst] = std::make_unique<SiluMatch>(sm);
+      fusions_.push_back("silu_gate: %" + dst->value().name + " = SiLU(%" +
+                         sm.g->value().name + ") * %" + sm.u->value().name);
+    } else if (MatchRms(dst, &rm)) {
+      rms_[dst] = std::make_unique<RmsMatch>(rm);
+      fusions_.push_back("rmsnorm: %" + dst->value().name + " = RMSNorm(%" +
+                         rm.x->value().name + ")");
+    }
+  }
+  // 3. router GEMMs that only feed moe_dispatch / moe_combine
+  for (const ir::OpNode* op : actions_) {
+    if (StartsWith(OpKey(op), "task.comm.")) continue;
+    const ir::ValueNode* dst = op->results()[0];
+    Slot& src = slot(producer_[dst]);
+    if (src.kind != Slot::kMma || src.args.size() != 2) continue;
+    const Buffer& b = slot(BaseGlobal(src.args[1])).buf;
+    const Buffer& a = slot(BaseGlobal(src.args[0])).buf;
+    if (b.shape.size() != 2 || b.shape[1] > 64 || b.dtype != Dtype::kBf16 ||
+        a.dtype != Dtype::kBf16 || slot(dst).buf.dtype != Dtype::kF32 ||
+        a.shape.size() != 2 || a.shape[1] % 8 != 0)
+      continue;
+    bool ok = !consumers_[dst].empty();
+    for (const ir::OpNode* c : consumers_[dst]) {
+      const std::string n = c->op().op.name;
+      if ((n != "comm.moe_dispatch" && n != "comm.moe_combine") || c->operands()[1] != dst ||
+          c->operands()[0] == dst)
+        ok = false;
+    }
+    for (const ir::ValueNode* o : task_.root()->outputs())
+      if (BaseGlobal(o) == dst) ok = false;
+    if (ok) {
+      router_[dst] = {BaseGlobal(src.args[0]), BaseGlobal(src.args[1])};
+      fusions_.push_back("router: %" + dst->value().name + " = router GEMM + top-k");
+    }
+  }
+}
+
+void Executor::Plan() {
+  if (analyzed_) return;
+  Analyze();
+  Fuse();
+  analyzed_ = true;
+}
+
+void Executor::Prepare() {
+  if (prepared_) return;
+  Plan();
+  const ir::Block* root = task_.root();
+  for (std::size_t i = 0; i < root->arguments().size(); ++i) {
+    inputs_[i].ptr = Alloc(inputs_[i].bytes());
+    slot(root->arguments()[i]).buf.ptr = inputs_[i].ptr;
+  }
+  for (const ir::OpNode* op : actions_) {
+    const ir::ValueNode* res = op->results()[0];
+    if (StartsWith(OpKey(op), "task.comm.")) {
+      PlanComm(op);
+    } else if (inlined_.count(res) || elided_.count(res)) {
+      continue;  // computed inside its consumer's launch
+    } else if (silu_.count(res)) {
+      PlanSilu(res);
+    } else if (rms_.count(res)) {
+      PlanRms(res);
+    } else if (router_.count(res)) {
+      Materialize(res);  // logits; the fused router launches with the dispatch
+    } else {
+      PlanStore(producer_[res], res);
+    }
+  }
+  for (const ir::ValueNode* o : task_.root()->outputs()) outputs_.push_back(GlobalOf(o));
   prepared_ = true;
+}
+
+void Executor::PlanSilu(const ir::ValueNode* dst) {
+  const SiluMatch& m = *silu_[dst];
+  Slot& mg = slot(producer_[m.g]);
+  Slot& mu = slot(producer_[m.u]);
+  const Buffer A = GlobalOf(mg.args[0]);
+  const Buffer Wg = GlobalOf(mg.args[1]);
+  const Buffer Wu = GlobalOf(mu.args[1]);
+  Buffer& out = Materialize(dst);
+  const int64_t K = A.shape[1], F = Wg.shape.back();
+  const int64_t E = Wg.shape.size() == 3 ? Wg.shape[0] : 1;
+  const int64_t M = A.shape[0];
+  if (Wg.shape[Wg.shape.size() - 2] != K) Fail("SiLU-gate GEMM: B rows must equal K");
+  void* w13 = Alloc(2 * E * F * K * 2);
+  const void* wg = Wg.ptr;
+  const void* wu = Wu.ptr;
+  once_steps_.push_back([=](cudaStream_t st) {
+    return kvm_sm100_pack_gate_up(wg, wu, w13, int(E), int(F), int(K), KVM_B_KN, st);
+  });
+  const void* a = A.ptr;
+  void* d = out.ptr;
+  Routing* r = slot(BaseGlobal(mg.args[0])).group;
+  if (Wg.shape.size() == 3) {
+    if (!r || r->E != E) Fail("per-expert SiLU-gate GEMM needs A grouped by a moe_dispatch");
+    steps_.push_back([=](cudaStream_t st) {
+      return kvm_sm100_grouped_gemm_bf16(a, w13, d, r->offsets, int(E), int(M),
+                                         int(2 * F), int(K), 2, st);
+    });
+    step_names_.push_back("grouped_gemm_silu_gate");
+  } else {
+    steps_.push_back([=](cudaStream_t st) {
+      return kvm_sm100_gemm_bf16_silu_gate(a, K, w13, d, F, int(M), int(F), int(K), st);
+    });
+    step_names_.push_back("gemm_silu_gate");
+  }
+}
+
+void Executor::PlanRms(const ir::ValueNode* dst) {
+  const RmsMatch& m = *rms_[dst];
+  const Buffer X = GlobalOf(m.x);
+  const void* g = m.gamma ? GlobalOf(m.gamma).ptr : nullptr;
+  Buffer& out = Materialize(dst);
+  const void* x = X.ptr;
+  void* y = out.ptr;
+  const int rows = int(X.shape[0]), H = int(X.shape[1]);
+  const float eps = m.eps;
+  steps_.push_back([=](cudaStream_t st) {
+    return kvm_sm100_rmsnorm_bf16(x, g, y, rows, H, eps, st);
+  });
+  step_names_.push_back("rmsnorm");
 }
 
 void Executor::PlanStore(const ir::ValueNode* src, const ir::ValueNode* dst) {
   Slot& s = slot(src);
-  Routing* group = s.group;
   Buffer& out = Materialize(dst);
-  slot(dst).group = group;
   if (s.kind == Slot::kMma) {
     PlanGemm(src, out);
   } else if (s.kind == Slot::kExpr) {
@@ -326,7 +661,15 @@ void Executor::PlanExpr(const ir::ValueNode* expr, const Buffer& out) {
     if (it != reg_of.end()) return it->second;
     Slot& s = slot(v);
     int r;
-    if (s.kind != Slot::kExpr) {
+    const ir::ValueNode* gv = s.kind == Slot::kExpr ? nullptr : BaseGlobal(v);
+    if (gv && inlined_.count(gv)) {
+      // the producer's expression, rounded to the inlined value's dtype
+      r = gen(producer_[gv]);
+      const Dtype dt = slot(gv).buf.dtype;
+      if (dt == Dtype::kBf16) r = emit(KVM_EW_ROUND_BF16, r, 0);
+      else if (dt == Dtype::kF16) r = emit(KVM_EW_ROUND_F16, r, 0);
+      else if (dt == Dtype::kI32) r = emit(KVM_EW_TRUNC_I32, r, 0);
+    } else if (s.kind != Slot::kExpr) {
       const Buffer& b = GlobalOf(v);
       auto in = input_of.find(b.ptr);
       int slot_i;
@@ -403,7 +746,7 @@ void Executor::PlanComm(const ir::OpNode* op) {
     if (kop)
       if (const std::any* a = attrs_.Get(kop, "top_k"))
         if (const auto* v = std::any_cast<std::int64_t>(a)) k = int(*v);
-    auto r = std::make_unique<Routing>();
+    Routing* r = routing_by_op_.at(op);
     r->T = int(x.shape[0]);
     r->E = int(g.shape[1]);
     r->k = k;
@@ -417,17 +760,36 @@ void Executor::PlanComm(const ir::OpNode* op) {
     Buffer& out = Materialize(res);
     if (out.numel() != n * x.shape[1] || out.dtype != Dtype::kBf16)
       Fail("moe_dispatch result must be bf16 [T*top_k, H]");
-    Routing* rp = r.get();
-    slot(res).group = rp;
-    const void* gp = g.ptr;
+    Routing* rp = r;
+    void* gp = g.ptr;
     const int gd = EwDtype(g.dtype);
     const void* xp = x.ptr;
     void* dp = out.ptr;
     const int H = int(x.shape[1]);
-    steps_.push_back([=](cudaStream_t st) {
-      return kvm_sm100_moe_topk(gp, gd, rp->T, rp->E, rp->k, rp->idx, rp->w, st);
-    });
-    step_names_.push_back("moe_topk");
+    auto rt = router_.find(BaseGlobal(op->operands()[1]));
+    if (rt != router_.end()) {
+      // router GEMM + softmax + top-k in one kernel; its weight [H, E] is
+      // re-laid out once to [E, H]
+      const Buffer& ra = GlobalOf(rt->second.first);
+      const Buffer& rw = GlobalOf(rt->second.second);
+      const int RH = int(rw.shape[0]), RE = int(rw.shape[1]);
+      void* wt = Alloc(rw.bytes());
+      const void* wsrc = rw.ptr;
+      once_steps_.push_back([=](cudaStream_t st) {
+        return kvm_sm100_transpose_bf16(wsrc, wt, 1, RH, RE, st);
+      });
+      const void* ap = ra.ptr;
+      steps_.push_back([=](cudaStream_t st) {
+        return kvm_sm100_moe_router_topk(ap, wt, static_cast<float*>(gp), rp->idx, rp->w,
+                                         rp->T, RH, RE, rp->k, st);
+      });
+      step_names_.push_back("moe_router_topk");
+    } else {
+      steps_.push_back([=](cudaStream_t st) {
+        return kvm_sm100_moe_topk(gp, gd, rp->T, rp->E, rp->k, rp->idx, rp->w, st);
+      });
+      step_names_.push_back("moe_topk");
+    }
     steps_.push_back([=](cudaStream_t st) {
       return kvm_sm100_moe_permute(rp->idx, rp->T, rp->k, rp->E, rp->offsets, rp->pos,
                                    rp->src, rp->ws, st);
@@ -438,7 +800,6 @@ void Executor::PlanComm(const ir::OpNode* op) {
     });
     step_names_.push_back("moe_scatter_rows");
     routing_of_[g.ptr] = rp;
-    routings_.push_back(std::move(r));
     return;
   }
   if (name == "comm.moe_combine") {

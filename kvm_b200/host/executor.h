@@ -4,14 +4,21 @@
 //   kernel graph --TransformKernelToTask (the reference's pass, using the
 //   sm_100a Device target)--> task graph --Prepare--> launch plan --Run-->
 //
-// Prepare walks the task graph once. Each task value is a global buffer, a
-// view of one (task.tma.gmem_to_smem / task.lsu.gmem_to_reg), a pending
-// tensor-core product (task.tc.mma / task.tc.mma_acc) or a pending ALU/SFU
-// expression; stores (task.lsu.reg_to_gmem) and collectives turn them into
-// launches: a tcgen05 GEMM (grouped by expert after a moe_dispatch), the
-// elementwise interpreter, the MoE routing / dispatch / combine kernels. Every
-// device buffer is allocated in Prepare; Run only launches (no allocation,
-// no host synchronisation), so a Run can be timed or repeated.
+// Prepare walks the task graph in three passes:
+//   analysis  each task value is a global buffer, a view of one
+//             (task.tma.gmem_to_smem / task.lsu.gmem_to_reg), a pending
+//             tensor-core product (task.tc.mma / task.tc.mma_acc) or a pending
+//             ALU/SFU expression; uses of every global are counted;
+//   fusion    single-use elementwise results are inlined into their consumer
+//             (rounded to their declared dtype, so the graph's arithmetic is
+//             kept); the SiLU-gate composite over two GEMMs that share A
+//             becomes one gate/up GEMM with the activation in its epilogue;
+//             the RMSNorm composite becomes the RMSNorm kernel; a router GEMM
+//             that only feeds moe_dispatch / moe_combine becomes the fused
+//             router + top-k kernel;
+//   planning  stores and collectives, in program order, become launches.
+// Every device buffer is allocated in Prepare; Run only launches (no
+// allocation, no host synchronisation), so a Run can be timed or repeated.
 #pragma once
 
 #include <cuda_runtime.h>
@@ -52,8 +59,10 @@ class Executor {
   const std::vector<Buffer>& inputs() const { return inputs_; }
   const std::vector<std::string>& input_names() const { return input_names_; }
 
+  // Analysis and fusion only (no GPU needed); Prepare runs it first.
+  void Plan();
   // Allocate buffers and build the launch plan. Inputs are allocated here and
-  // may be filled (FillInput / CopyInput) before or after Prepare.
+  // may be filled (FillInput / CopyInput) after Prepare.
   void Prepare();
   void CopyInput(int index, const void* host, int64_t bytes);
   void FillInputNormal(int index, uint64_t seed, float mean, float std);
@@ -68,17 +77,31 @@ class Executor {
   const ir::Graph& task_graph() const { return task_; }
   int launches_per_run() const { return static_cast<int>(steps_.size()); }
   const std::vector<std::string>& step_names() const { return step_names_; }
+  // Fusions applied by Prepare, one line each (for reports and tests).
+  const std::vector<std::string>& fusions() const { return fusions_; }
 
  private:
   struct Slot;
   struct Routing;
+  struct SNode;
+  struct SiluMatch;
+  struct RmsMatch;
   Slot& slot(const ir::ValueNode* v);
   Buffer& Materialize(const ir::ValueNode* v);
   const Buffer& GlobalOf(const ir::ValueNode* v);
+  const ir::ValueNode* BaseGlobal(const ir::ValueNode* v);
+  void Analyze();
+  void Fuse();
+  SNode Resolve(const ir::ValueNode* v);
+  bool MatchSilu(const ir::ValueNode* dst, SiluMatch* m);
+  bool MatchRms(const ir::ValueNode* dst, RmsMatch* m);
+  bool InputFill(const ir::ValueNode* v, double* value) const;
   void PlanStore(const ir::ValueNode* src, const ir::ValueNode* dst);
   void PlanGemm(const ir::ValueNode* mma, const Buffer& out);
   void PlanExpr(const ir::ValueNode* expr, const Buffer& out);
   void PlanComm(const ir::OpNode* op);
+  void PlanSilu(const ir::ValueNode* dst);
+  void PlanRms(const ir::ValueNode* dst);
   void* Alloc(int64_t bytes);
   const ir::OpNode* KernelCommOp(const std::string& name, int nth) const;
 
@@ -92,9 +115,23 @@ class Executor {
   std::vector<std::unique_ptr<Routing>> routings_;
   std::vector<void*> allocations_;
   std::unordered_map<const void*, Routing*> routing_of_;  // logits buffer -> routing
+  // analysis / fusion state
+  std::vector<const ir::OpNode*> actions_;  // stores and collectives, in order
+  std::unordered_map<const ir::ValueNode*, const ir::ValueNode*> producer_;  // global <- stored value
+  std::unordered_map<const ir::ValueNode*, int> uses_;        // global -> reads
+  std::unordered_map<const ir::ValueNode*, std::vector<const ir::OpNode*>> consumers_;
+  std::unordered_map<const ir::OpNode*, Routing*> routing_by_op_;
+  std::unordered_map<const ir::ValueNode*, bool> inlined_;    // folded into a consumer
+  std::unordered_map<const ir::ValueNode*, bool> elided_;     // produced inside a fusion
+  std::unordered_map<const ir::ValueNode*, std::unique_ptr<SiluMatch>> silu_;
+  std::unordered_map<const ir::ValueNode*, std::unique_ptr<RmsMatch>> rms_;
+  std::unordered_map<const ir::ValueNode*, std::pair<const ir::ValueNode*, const ir::ValueNode*>>
+      router_;  // logits global -> (x, router weight [H, E]) of its fused GEMM
+  std::vector<std::string> fusions_;
   std::vector<std::function<int(cudaStream_t)>> once_steps_;  // weight re-layouts
   std::vector<std::function<int(cudaStream_t)>> steps_;
   std::vector<std::string> step_names_;
+  bool analyzed_ = false;
   bool prepared_ = false;
   bool once_done_ = false;
 };

@@ -127,9 +127,13 @@ int main(int argc, char** argv) {
       kvm::ir::task::RegisterTaskDialect(treg);
       std::cerr << kvm::ir::serial::Serialize(ex.task_graph(), treg);
     }
-    if (lower_only) {  // parse + lower only: no GPU needed
+    if (lower_only) {  // parse + lower + fusion analysis only: no GPU needed
+      ex.Plan();
       std::cout << "{\"graph\": \"" << graph_path << "\", \"task_ops\": "
-                << ex.task_graph().root()->operations().size() << "}" << std::endl;
+                << ex.task_graph().root()->operations().size() << ", \"fusions\": [";
+      for (std::size_t i = 0; i < ex.fusions().size(); ++i)
+        std::cout << (i ? ", " : "") << "\"" << ex.fusions()[i] << "\"";
+      std::cout << "]}" << std::endl;
       return 0;
     }
     ex.Prepare();
@@ -176,6 +180,9 @@ int main(int argc, char** argv) {
        << ", \"iters\": " << iters << ", \"steps\": [";
     for (std::size_t i = 0; i < ex.step_names().size(); ++i)
       js << (i ? ", " : "") << "\"" << ex.step_names()[i] << "\"";
+    js << "], \"fusions\": [";
+    for (std::size_t i = 0; i < ex.fusions().size(); ++i)
+      js << (i ? ", " : "") << "\"" << ex.fusions()[i] << "\"";
     js << "], \"outputs\": [";
     const auto& outs = kernel.root()->outputs();
     for (std::size_t i = 0; i < ex.outputs().size(); ++i) {

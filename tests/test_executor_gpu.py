@@ -22,7 +22,7 @@ def _t(dtype, shape):
     return f"kernel.tensor<dtype={dtype}, shape=[{','.join(map(str, shape))}]>"
 
 
-def _run(tmp_path, text, inputs, iters=2):
+def _run(tmp_path, text, inputs, iters=2, fuse=True):
     if not KVM_RUN.exists():
         pytest.fail("kvm_run is not built (python -c 'import __graft_entry__ as g; g.build()')")
     g = tmp_path / "g.kvm"
@@ -32,9 +32,11 @@ def _run(tmp_path, text, inputs, iters=2):
     outd.mkdir()
     for name, arr in inputs.items():
         np.ascontiguousarray(arr).tofile(ind / f"{name}.bin")
+    import os
+    env = dict(os.environ, KVM_EXEC_NO_FUSION="0" if fuse else "1")
     r = subprocess.run([str(KVM_RUN), str(g), "--inputs", str(ind), "--out", str(outd),
                         "--warmup", "1", "--iters", str(iters)],
-                       capture_output=True, text=True, timeout=300)
+                       capture_output=True, text=True, timeout=300, env=env)
     assert r.returncode == 0, r.stderr
     summary = json.loads(r.stdout.strip().splitlines()[-1])
     return summary, outd
@@ -126,7 +128,8 @@ def test_elementwise_broadcast_graph(cuda, tmp_path):
     assert np.array_equal(k, (_f(x) > _f(y)).astype(np.float32))
 
 
-def test_moe_graph(cuda, tmp_path):
+@pytest.mark.parametrize("fuse", [True, False])
+def test_moe_graph(cuda, tmp_path, fuse):
     rng = np.random.default_rng(2)
     T, H, E, F, k = 512, 256, 8, 128, 2
     x = oracle.normal_bf16(rng, (T, H))
@@ -153,8 +156,10 @@ def test_moe_graph(cuda, tmp_path):
   }}
 }}"""
     s, outd = _run(tmp_path, text, {"x": x, "wr": wr, "w1": w1, "w3": w3, "w2": w2,
-                                    "one": one})
+                                    "one": one}, fuse=fuse)
+    # g is also a graph output, so the router GEMM is not fused into top-k
     assert s["steps"][:4] == ["gemm_bf16", "moe_topk", "moe_permute", "moe_scatter_rows"]
+    assert ("grouped_gemm_silu_gate" in s["steps"]) == fuse
     g = np.fromfile(outd / "g.bin", dtype=np.float32).reshape(T, E)
     assert rel_err(g, oracle.gemm(x, wr, out_f32=True)) < 1e-5
     # oracle composed op by op, routed on the GPU's own logits
@@ -175,7 +180,8 @@ def test_moe_graph(cuda, tmp_path):
     assert rel_err(_f(out), _f(ref)) < 1e-2
 
 
-def test_rmsnorm_mlp_graph(cuda, tmp_path):
+@pytest.mark.parametrize("fuse", [True, False])
+def test_rmsnorm_mlp_graph(cuda, tmp_path, fuse):
     rng = np.random.default_rng(3)
     T, H, F = 256, 512, 1024
     x = oracle.normal_bf16(rng, (T, H))
@@ -188,8 +194,11 @@ def test_rmsnorm_mlp_graph(cuda, tmp_path):
     wd = oracle.normal_bf16(rng, (F, H), 0.05)
     text = mlp_graph(T, H, F)
     s, outd = _run(tmp_path, text, {"x": x, "gamma": gamma, "invh": invh, "eps": eps,
-                                    "one": one, "wg": wg, "wu": wu, "wd": wd})
-    assert "gemv_bf16" in s["steps"]
+                                    "one": one, "wg": wg, "wu": wu, "wd": wd}, fuse=fuse)
+    if fuse:
+        assert s["steps"] == ["rmsnorm", "gemm_silu_gate", "gemm_bf16"]
+    else:
+        assert "gemv_bf16" in s["steps"] and len(s["steps"]) == 14
     sq = _bf(_f(x) * _f(x))
     ms = oracle.gemm(sq, invh, out_f32=True)          # [T, 1]
     r = 1.0 / np.sqrt(ms + eps[0])
@@ -205,3 +214,26 @@ def test_rmsnorm_mlp_graph(cuda, tmp_path):
     ref = oracle.gemm(h, wd)
     o = np.fromfile(outd / "o.bin", dtype=np.uint16).reshape(T, H)
     assert rel_err(_f(o), _f(ref)) < 1e-2
+
+
+def test_moe_graph_router_fused(cuda, tmp_path):
+    """With the logits only feeding dispatch/combine, the router GEMM, softmax
+    and top-k run as one kernel; results match the unfused run."""
+    rng = np.random.default_rng(4)
+    T, H, E, F, k = 256, 256, 16, 128, 2
+    ins = {"x": oracle.normal_bf16(rng, (T, H)), "wr": oracle.normal_bf16(rng, (H, E), 0.05),
+           "w1": oracle.normal_bf16(rng, (E, H, F), 0.05),
+           "w3": oracle.normal_bf16(rng, (E, H, F), 0.05),
+           "w2": oracle.normal_bf16(rng, (E, F, H), 0.05), "one": _bf(np.ones(1))}
+    text = (ROOT / "kvm_b200" / "graphs" / "moe_layer.kvm").read_text()
+    for a, b in [("[8192,4096]", f"[{T},{H}]"), ("[4096,64]", f"[{H},{E}]"),
+                 ("[64,4096,1408]", f"[{E},{H},{F}]"), ("[64,1408,4096]", f"[{E},{F},{H}]"),
+                 ("[8192,64]", f"[{T},{E}]"), ("[16384,4096]", f"[{T * k},{H}]"),
+                 ("[16384,1408]", f"[{T * k},{F}]")]:
+        text = text.replace(a, b)
+    s1, o1 = _run(tmp_path / "a", text, ins) if (tmp_path / "a").mkdir() is None else None
+    s2, o2 = _run(tmp_path / "b", text, ins, fuse=False) if (tmp_path / "b").mkdir() is None else None
+    assert s1["steps"][0] == "moe_router_topk" and s2["steps"][0] == "gemm_bf16"
+    a = _f(np.fromfile(o1 / "out.bin", dtype=np.uint16))
+    b = _f(np.fromfile(o2 / "out.bin", dtype=np.uint16))
+    assert rel_err(a, b) < 1e-2

@@ -32,14 +32,18 @@ def test_reference_tests_pass_on_sm100_device(host_bin, name):
     assert "all tests passed" in r.stdout
 
 
-@pytest.mark.parametrize("graph,ops", [("matmul_1024", 4), ("moe_layer", 37),
-                                       ("mlp_block", 54)])
-def test_config_graphs_lower(host_bin, graph, ops):
+@pytest.mark.parametrize("graph,ops,fusions", [
+    ("matmul_1024", 4, []),
+    ("moe_layer", 37, ["silu_gate", "router"]),
+    ("mlp_block", 54, ["rmsnorm", "silu_gate"])])
+def test_config_graphs_lower(host_bin, graph, ops, fusions):
     r = subprocess.run([str(host_bin / "kvm_run"), str(GRAPHS / f"{graph}.kvm"),
                         "--lower-only", "--dump-task"], capture_output=True, text=True,
                        timeout=60)
     assert r.returncode == 0, r.stderr
-    assert json.loads(r.stdout)["task_ops"] == ops
+    out = json.loads(r.stdout)
+    assert out["task_ops"] == ops
+    assert [f.split(":")[0] for f in out["fusions"]] == fusions
     # the dump is itself a parseable task graph with the expected units
     assert "task.tc.mma" in r.stderr and "loc=shared" in r.stderr
 
@@ -56,3 +60,11 @@ def test_unlowerable_op_fails_loudly(host_bin, tmp_path):
     r = subprocess.run([str(host_bin / "kvm_run"), str(g), "--lower-only"],
                        capture_output=True, text=True, timeout=60)
     assert r.returncode != 0
+
+
+def test_fusion_can_be_disabled(host_bin):
+    import os
+    env = dict(os.environ, KVM_EXEC_NO_FUSION="1")
+    r = subprocess.run([str(host_bin / "kvm_run"), str(GRAPHS / "moe_layer.kvm"),
+                        "--lower-only"], capture_output=True, text=True, timeout=60, env=env)
+    assert r.returncode == 0 and json.loads(r.stdout)["fusions"] == []
