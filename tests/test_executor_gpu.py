@@ -57,7 +57,7 @@ def mlp_graph(T, H, F):
     bf, f32 = "bf16", "f32"
     return f"""graph {{
   config {{ ranks = [0] }}
-  ^mlp(%x: {_t(bf, [T, H])}, %gamma: {_t(bf, [H])}, %invh: {_t(bf, [H, 1])}, %eps: {_t(f32, [1])}, %one: {_t(bf, [1])}, %wg: {_t(bf, [H, F])}, %wu: {_t(bf, [H, F])}, %wd: {_t(bf, [F, H])}) {{
+  ^mlp(%x: {_t(bf, [T, H])}, %gamma: {_t(bf, [H])}, %invh: {_t(bf, [H, 1])} {{fill = {1.0 / H!r}}}, %eps: {_t(f32, [1])} {{fill = 1e-5}}, %one: {_t(bf, [1])} {{fill = 1.0}}, %wg: {_t(bf, [H, F])}, %wu: {_t(bf, [H, F])}, %wd: {_t(bf, [F, H])}) {{
     %sq: {_t(bf, [T, H])} = kernel.mul(%x, %x)
     %ms: {_t(f32, [T, 1])} = kernel.matmul(%sq, %invh)
     %ve: {_t(f32, [T, 1])} = kernel.add(%ms, %eps)
@@ -140,7 +140,7 @@ def test_moe_graph(cuda, tmp_path, fuse):
     one = _bf(np.ones(1))
     text = f"""graph {{
   config {{ ranks = [0] }}
-  ^moe(%x: {_t('bf16', [T, H])}, %wr: {_t('bf16', [H, E])}, %w1: {_t('bf16', [E, H, F])}, %w3: {_t('bf16', [E, H, F])}, %w2: {_t('bf16', [E, F, H])}, %one: {_t('bf16', [1])}) {{
+  ^moe(%x: {_t('bf16', [T, H])}, %wr: {_t('bf16', [H, E])}, %w1: {_t('bf16', [E, H, F])}, %w3: {_t('bf16', [E, H, F])}, %w2: {_t('bf16', [E, F, H])}, %one: {_t('bf16', [1])} {{fill = 1.0}}) {{
     %g: {_t('f32', [T, E])} = kernel.matmul(%x, %wr)
     %d: {_t('bf16', [T * k, H])} = kernel.comm.moe_dispatch<ranks=[0]> {{top_k = {k}}} (%x, %g)
     %a: {_t('bf16', [T * k, F])} = kernel.matmul(%d, %w1)
