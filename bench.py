@@ -45,7 +45,7 @@ def parse_args(argv=None):
     ap = argparse.ArgumentParser(description=__doc__,
                                  formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--steps", type=int, default=1500)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true",
@@ -302,7 +302,7 @@ def run_ours(args) -> int:
                 "peak": pk["hbm"], "unit": "GB/s"}
     roof["frac"] = roof["achieved"] / roof["peak"]
     roof["traffic"] = traffic
-    roof["kernel"] = "grouped gate/up GEMM + fused SiLU-gate (gemm_bf16_kernel<256,4,false,2>)"
+    roof["kernel"] = "grouped gate/up GEMM + fused SiLU-gate on SM pairs (gemm_pair_kernel<2>)"
     roof["algorithmic"] = {"flop": flops, "bytes": bytes_alg, "ms": gemm_ms,
                            "peak_src": pk["src"] + " (sustained bf16)"}
 
@@ -339,7 +339,7 @@ def run_ours(args) -> int:
 def profile_traffic():
     """DRAM bytes per launch of the dominant kernel from the committed ncu
     summary (a `traffic_bytes_per_launch:` line), or None."""
-    p = ROOT / "profiles" / "moe_gemm13_T8192.md"
+    p = ROOT / "profiles" / "moe_pair_gemm_T8192.md"
     if not p.exists():
         return None
     for line in p.read_text().splitlines():

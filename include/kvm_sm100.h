@@ -74,15 +74,16 @@ int kvm_sm100_gemm_bf16(const void* A, int64_t lda, const void* B,
 
 /* H[M, F] = bf16( SiLU(A.Wg^T) * (A.Wu^T) ), the gated-FFN front half with
  * the activation fused into the GEMM epilogue. W13 is the packed weight from
- * kvm_sm100_pack_gate_up ([2F, K], gate/up interleaved in 128-row blocks).
+ * kvm_sm100_pack_gate_up ([2F, K], gate/up interleaved in 64-row blocks).
  * Replaces the composite kernel.matmul x2 -> neg/exp/add/div/mul chain. */
 int kvm_sm100_gemm_bf16_silu_gate(const void* A, int64_t lda, const void* W13,
                                   void* H, int64_t ldh, int M, int F, int K,
                                   kvm_stream_t stream);
 
 /* Pack G groups of gate/up weights into the interleaved layout consumed by
- * the *_silu_gate GEMMs: out[g] = [Wg[g][0:128]; Wu[g][0:128]; Wg[g][128:256];
- * ...], each block 128 rows of K. w_layout says how Wg/Wu are stored:
+ * the *_silu_gate GEMMs: out[g] = [Wg[g][0:64]; Wu[g][0:64]; Wg[g][64:128];
+ * ...], each block 64 rows of K (one SM of a GEMM SM pair holds the gate and
+ * the up rows of the same 64 f). w_layout says how Wg/Wu are stored:
  * KVM_B_NK = [G, F, K], KVM_B_KN = [G, K, F] (transposed while packing).
  * F must be a multiple of 128. */
 int kvm_sm100_pack_gate_up(const void* Wg, const void* Wu, void* out, int G,

@@ -111,7 +111,7 @@ __global__ void __launch_bounds__(256)
 // given by out_row(c). 32x32 tiles through shared memory; both the global
 // reads (along C) and the writes (along R) are coalesced.
 //   mode 0: out_row(c) = c,            out rows per group = C
-//   mode 1: gate/up interleave: out_row(c) = (c/128)*256 + which*128 + c%128,
+//   mode 1: gate/up interleave: out_row(c) = (c/64)*128 + which*64 + c%64,
 //           out rows per group = 2C
 __global__ void transpose_kernel(const uint16_t* __restrict__ in,
                                  uint16_t* __restrict__ out, int R, int C,
@@ -130,7 +130,7 @@ __global__ void transpose_kernel(const uint16_t* __restrict__ in,
     const int c = c0 + i, r = r0 + threadIdx.x;
     if (r < R && c < C) {
       const long long orow =
-          mode == 0 ? c : (c / 128) * 256 + which * 128 + (c % 128);
+          mode == 0 ? c : (c / 64) * 128 + which * 64 + (c % 64);
       dst[orow * R + r] = tile[threadIdx.x][i];
     }
   }
@@ -147,9 +147,9 @@ __global__ void pack_rows_kernel(const uint4* __restrict__ wg,
     const int col = static_cast<int>(v - orow * row_vecs);
     const long long g = orow / (2ll * F);
     const int r = static_cast<int>(orow - g * 2ll * F);
-    const int blk = r / 256, i = r % 256;
-    const int f = blk * 128 + (i % 128);
-    const uint4* src = i < 128 ? wg : wu;
+    const int blk = r / 128, i = r % 128;
+    const int f = blk * 64 + (i % 64);
+    const uint4* src = i < 64 ? wg : wu;
     out[v] = __ldg(src + (g * F + f) * row_vecs + col);
   }
 }

@@ -1,7 +1,12 @@
 // Host launchers of the bf16 tcgen05 GEMM: dense GEMM (kernel.matmul /
 // kernel.gemm), the fused SiLU-gate GEMM, the grouped expert GEMM and the
 // router GEMM with fused softmax/top-k.
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
+
 #include "gemm_bf16.cuh"
+#include "gemm_pair.cuh"
 #include "runtime.h"
 
 namespace kvm {
@@ -17,6 +22,97 @@ int launch(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p,
   kern<<<grid, kGemmThreads, smem, st>>>(ta, tb, p);
   KVM_CUDA_TRY(cudaGetLastError());
   return KVM_OK;
+}
+
+// SM pairs that can be resident at once for the pair kernel (clusters of 2
+// need two free SMs of one GPC), cached per device and epilogue.
+template <int EPI>
+int pair_clusters(int* out) {
+  static std::mutex mu;
+  static int cached[64] = {0};
+  int dev = 0;
+  KVM_CUDA_TRY(cudaGetDevice(&dev));
+  std::lock_guard<std::mutex> lock(mu);
+  if (dev >= 0 && dev < 64 && cached[dev] > 0) {
+    *out = cached[dev];
+    return KVM_OK;
+  }
+  auto kern = gemm_pair_kernel<EPI>;
+  constexpr size_t smem = gemm_pair_smem_bytes();
+  KVM_CUDA_TRY(cudaFuncSetAttribute(
+      kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
+  const DeviceInfo* d = device_info();
+  if (!d) return KVM_ERR_CUDA;
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(2 * (d->sm_count / 2));
+  cfg.blockDim = dim3(kPairThreads);
+  cfg.dynamicSmemBytes = smem;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  KVM_CUDA_TRY(cudaOccupancyMaxActiveClusters(&n, kern, &cfg));
+  if (n <= 0) return fail(KVM_ERR_UNSUPPORTED, "pair GEMM: no SM pair can be resident");
+  if (n > d->sm_count / 2) n = d->sm_count / 2;
+  if (dev >= 0 && dev < 64) cached[dev] = n;
+  *out = n;
+  return KVM_OK;
+}
+
+// Launch the pair kernel on min(resident pairs, upper bound of pair tiles).
+template <int EPI>
+int launch_pair(const PairMaps& maps, const PairParams& p, long long max_tiles,
+                cudaStream_t st) {
+  int ncl = 0;
+  int rc = pair_clusters<EPI>(&ncl);
+  if (rc != KVM_OK) return rc;
+  if (max_tiles < ncl) ncl = int(max_tiles > 0 ? max_tiles : 1);
+  auto kern = gemm_pair_kernel<EPI>;
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(2 * ncl);
+  cfg.blockDim = dim3(kPairThreads);
+  cfg.dynamicSmemBytes = gemm_pair_smem_bytes();
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  KVM_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, maps, p));
+  return KVM_OK;
+}
+
+// Tensor maps of the pair kernel: weights [G*N, K] in 128-row boxes, tokens
+// [rows, K] (row stride lda) in boxes of 128, 64, 32, 16 and 8 rows.
+int encode_pair_maps(PairMaps* m, const void* X, long long lda, int rows,
+                     const void* W, long long wrows, int K) {
+  int rc = encode_tmap_2d(&m->w, W, K, wrows, (uint64_t)K * 2, kPairBK, 128,
+                          CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
+                          CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc != KVM_OK) return rc;
+  for (int i = 0; i < 5; ++i) {
+    rc = encode_tmap_2d(&m->x[i], X, K, rows, (uint64_t)lda * 2, kPairBK,
+                        128u >> i, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
+                        CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc != KVM_OK) return rc;
+  }
+  return KVM_OK;
+}
+
+// The SM-pair kernel serves the grouped and SiLU-gate GEMMs unless
+// KVM_SM100_PAIR_GEMM=0 selects the one-SM kernel (for comparison).
+bool pair_enabled() {
+  static const bool on = [] {
+    const char* e = std::getenv("KVM_SM100_PAIR_GEMM");
+    return !(e && std::strcmp(e, "0") == 0);
+  }();
+  return on;
 }
 
 int check_ptr(const void* p, const char* what) {
@@ -136,7 +232,23 @@ static int grouped_impl(const void* A, long long lda, const void* B, void* D,
   p.D = D; p.ldd = ldd; p.C = nullptr; p.ldc = 0;
   p.status = dev->status;
 
-  constexpr int BN = 256;
+  if (pair_enabled()) {
+    PairParams pp{};
+    pp.rows = rows; pp.N = N; pp.K = K;
+    pp.num_groups = G; pp.offsets = offsets;
+    pp.D = D; pp.ldd = ldd; pp.C = nullptr; pp.ldc = 0;
+    pp.status = dev->status;
+    PairMaps maps;
+    KVM_TRY(encode_pair_maps(&maps, A, lda, rows, B, (long long)N * G, K));
+    // every group has at most rows/256 + 1 token tiles
+    const long long ub = (long long)(cdiv(rows, kPairMaxTN) + G) * cdiv(N, 256);
+    if (epilogue == kEpiSilu) return launch_pair<kEpiSilu>(maps, pp, ub, st);
+    return launch_pair<kEpiBf16>(maps, pp, ub, st);
+  }
+
+  // One-SM kernel: SiLU-gate tiles of 128 columns hold one 64-row gate block
+  // and its up block.
+  const int BN = epilogue == kEpiSilu ? 128 : 256;
   const long long ub = (long long)(cdiv(rows, kGemmBM) + G) * cdiv(N, BN);
   const int grid = ub < dev->sm_count ? int(ub) : dev->sm_count;
   CUtensorMap ta, tb;
@@ -147,8 +259,8 @@ static int grouped_impl(const void* A, long long lda, const void* B, void* D,
                          BN, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
                          CU_TENSOR_MAP_SWIZZLE_128B));
   if (epilogue == kEpiSilu)
-    return launch<BN, 4, false, kEpiSilu>(ta, tb, p, grid, st);
-  return launch<BN, 4, false, kEpiBf16>(ta, tb, p, grid, st);
+    return launch<128, 6, false, kEpiSilu>(ta, tb, p, grid, st);
+  return launch<256, 4, false, kEpiBf16>(ta, tb, p, grid, st);
 }
 
 extern "C" int kvm_sm100_gemm_bf16_silu_gate(const void* A, int64_t lda,

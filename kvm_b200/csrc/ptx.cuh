@@ -254,6 +254,147 @@ __device__ __forceinline__ uint64_t sdesc_sw128(uint32_t start, uint32_t lbo,
   return d;
 }
 
+// ---------------------------------------------------------------- CTA pairs
+//
+// A cluster of two CTAs on two SMs issues one tcgen05.mma.cta_group::2: the
+// even CTA (rank 0) issues it, each CTA holds half of A (M/2 rows) and half
+// of B (N/2 rows) at the same shared-memory offsets, and each CTA's TMEM
+// receives its M/2 rows of D. Barriers of the other CTA are addressed through
+// the shared::cluster window (mapa).
+
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+__device__ __forceinline__ uint32_t cluster_id_x() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%clusterid.x;" : "=r"(r));
+  return r;
+}
+
+__device__ __forceinline__ uint32_t nclusters_x() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%nclusterid.x;" : "=r"(r));
+  return r;
+}
+
+// shared::cluster address of the variable at shared::cta address `addr` in
+// CTA `rank` of this cluster.
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;"
+               : "=r"(r)
+               : "r"(addr), "r"(rank));
+  return r;
+}
+
+// Every thread of both CTAs; orders shared-memory writes (barrier init) of
+// each CTA before the other's later accesses.
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile(
+      "barrier.cluster.arrive.release.aligned;\n\t"
+      "barrier.cluster.wait.acquire.aligned;" ::
+          : "memory");
+}
+
+// Arrive on an mbarrier that may live in the other CTA of the cluster.
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
+  asm volatile(
+      "mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(
+          cluster_addr)
+      : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar,
+                                                      uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait for a phase completed by arrivals from either CTA.
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity,
+                                                  volatile int* abort) {
+  if (mbar_try_wait_cluster(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t i = 1;; ++i) {
+    if (mbar_try_wait_cluster(bar, parity)) return true;
+    if ((i & 63u) == 0) {
+      if (*abort) return false;
+      if (globaltimer_ns() - t0 > kWaitTimeoutNs) {
+        *abort = 1;
+        return false;
+      }
+    }
+  }
+}
+
+// 2-D TMA load into this CTA's shared memory whose transaction bytes are
+// counted on an mbarrier of either CTA of the pair (`bar_cluster`). No
+// multicast: each CTA loads only its own half of the operands.
+__device__ __forceinline__ void tma_load_2d_pair(void* dst, const void* tmap,
+                                                 uint32_t bar_cluster,
+                                                 int32_t x, int32_t y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::"
+      "complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(tmap), "r"(bar_cluster), "r"(x), "r"(y)
+      : "memory");
+}
+
+// TMEM allocation shared by the pair: one warp of each CTA (same warp index)
+// executes it; both CTAs receive the same column range.
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t* dst, uint32_t ncols) {
+  asm volatile(
+      "tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+          smem_u32(dst)),
+      "r"(ncols)
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_relinquish_pair() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::
+                   : "memory");
+}
+
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(
+                   taddr),
+               "r"(ncols)
+               : "memory");
+}
+
+// D (both CTAs' TMEM) (+)= A x B^T over the pair, kind::f16; issued by one
+// thread of the even CTA.
+__device__ __forceinline__ void mma_f16_ss_pair(uint32_t d_tmem, uint64_t a_desc,
+                                                uint64_t b_desc, uint32_t idesc,
+                                                uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(
+          d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Arrive once on the mbarrier at `bar_cluster` (either CTA) when every pair
+// MMA issued so far by this thread has completed.
+__device__ __forceinline__ void mma_commit_pair(uint32_t bar_cluster) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 "
+      "[%0];" ::"r"(bar_cluster)
+      : "memory");
+}
+
 // Instruction descriptor, kind::f16 with bf16 A/B and fp32 accumulator.
 // a_mn / b_mn select MN-major (1) or K-major (0) operands.
 __host__ __device__ constexpr uint32_t idesc_bf16(int m, int n, int a_mn,

@@ -90,7 +90,7 @@ def gemm(a: torch.Tensor, b: torch.Tensor, c: torch.Tensor, **kw) -> torch.Tenso
 
 
 def pack_gate_up(w_gate: torch.Tensor, w_up: torch.Tensor, layout: str = "nk") -> torch.Tensor:
-    """Interleave gate/up weights in 128-row blocks for the SiLU-gate GEMMs.
+    """Interleave gate/up weights in 64-row blocks for the SiLU-gate GEMMs.
 
     layout "nk": inputs [G, F, K] (or [F, K]); "kn": inputs [G, K, F] (or [K, F]).
     Returns [G, 2F, K] (or [2F, K]).

@@ -126,7 +126,7 @@ def gemm_silu_gate(a: np.ndarray, wg: np.ndarray, wu: np.ndarray) -> np.ndarray:
 
 
 def pack_gate_up(wg: np.ndarray, wu: np.ndarray) -> np.ndarray:
-    """[G, F, K] gate/up -> [G, 2F, K] interleaved in 128-row blocks."""
+    """[G, F, K] gate/up -> [G, 2F, K] interleaved in 64-row blocks."""
     wg, wu = _c(wg, np.uint16), _c(wu, np.uint16)
     G, F, K = wg.shape
     out = np.empty((G, 2 * F, K), dtype=np.uint16)

@@ -163,15 +163,15 @@ void orc_gemm_silu_gate(const uint16_t* A, const uint16_t* Wg,
   free(u);
 }
 
-/* Gate/up packing: out[g] rows = [Wg[g][0:128]; Wu[g][0:128]; Wg[g][128:256];
- * ...], inputs [G][F][K]. */
+/* Gate/up packing: out[g] rows = [Wg[g][0:64]; Wu[g][0:64]; Wg[g][64:128];
+ * ...], 64-row blocks, inputs [G][F][K]. */
 void orc_pack_gate_up(const uint16_t* Wg, const uint16_t* Wu, uint16_t* out,
                       int G, int F, int K) {
   for (int g = 0; g < G; ++g)
     for (int r = 0; r < 2 * F; ++r) {
-      int blk = r / 256, i = r % 256;
-      int f = blk * 128 + (i % 128);
-      const uint16_t* src = (i < 128 ? Wg : Wu) + ((int64_t)g * F + f) * K;
+      int blk = r / 128, i = r % 128;
+      int f = blk * 64 + (i % 64);
+      const uint16_t* src = (i < 64 ? Wg : Wu) + ((int64_t)g * F + f) * K;
       memcpy(out + ((int64_t)g * 2 * F + r) * K, src, sizeof(uint16_t) * K);
     }
 }
@@ -271,7 +271,7 @@ void orc_moe_scatter_rows(const uint16_t* x, const int32_t* pos, uint16_t* xp,
 
 /* Grouped GEMM over permuted rows: for group g, rows [off[g], off[g+1]) of A
  * times W[g]^T (W stored [G][N][K]). silu_gate = 1: W is packed gate/up
- * ([G][2F][K], 128-row blocks) and D[r][0:F] = bf16(SiLU(g) * u). */
+ * ([G][2F][K], 64-row blocks) and D[r][0:F] = bf16(SiLU(g) * u). */
 void orc_grouped_gemm_bf16(const uint16_t* A, const uint16_t* W, uint16_t* D,
                            const int32_t* off, int G, int N, int K,
                            int silu_gate) {
@@ -290,9 +290,9 @@ void orc_grouped_gemm_bf16(const uint16_t* A, const uint16_t* W, uint16_t* D,
 #pragma omp parallel for schedule(static)
       for (int i = 0; i < M; ++i)
         for (int f = 0; f < F; ++f) {
-          int blk = f / 128, c = f % 128;
-          float gv = acc[(int64_t)i * N + blk * 256 + c];
-          float uv = acc[(int64_t)i * N + blk * 256 + 128 + c];
+          int blk = f / 64, c = f % 64;
+          float gv = acc[(int64_t)i * N + blk * 128 + c];
+          float uv = acc[(int64_t)i * N + blk * 128 + 64 + c];
           D[((int64_t)r0 + i) * F + f] = f2bf(silu(gv) * uv);
         }
     }

@@ -77,8 +77,10 @@ def test_gemm_silu_gate_and_packing():
     wu = oracle.normal_bf16(rng, (1, F, K))
     h = oracle.gemm_silu_gate(a, wg[0], wu[0])
     w13 = oracle.pack_gate_up(wg, wu)
-    assert np.array_equal(w13[0, 128:256], wu[0, 0:128])
-    assert np.array_equal(w13[0, 256:384], wg[0, 128:256])
+    assert np.array_equal(w13[0, 0:64], wg[0, 0:64])
+    assert np.array_equal(w13[0, 64:128], wu[0, 0:64])
+    assert np.array_equal(w13[0, 128:192], wg[0, 64:128])
+    assert np.array_equal(w13[0, 448:512], wu[0, 192:256])
     off = np.array([0, M], dtype=np.int32)
     h2 = oracle.grouped_gemm(a, w13, off, silu_gate=True)
     assert np.array_equal(h, h2)
