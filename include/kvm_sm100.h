@@ -289,10 +289,13 @@ int kvm_sm100_silu_mul_bf16(const void* g, const void* u, void* h, int64_t n,
  * sequences. Tokens are rows b*L + pos; q/out hold HQ heads of 128 columns
  * each, k/v hold HKV heads (q head h reads kv head h / (HQ/HKV)); row strides
  * ldq, ldk, ldv, ldo in elements (bf16). Per head:
- *   S = scale * Q K^T (fp32), P = softmax over keys <= pos (fp32 statistics,
- *   P rounded to bf16), O = P V (fp32 accumulate, bf16 out).
+ *   S = scale * Q K^T (fp32), P = softmax over keys <= pos, O = P V
+ *   (fp32 accumulate, bf16 out), computed in one fused pass per 128-query
+ *   tile: running max and sum in fp32, unnormalised P rounded to bf16 for
+ *   the P.V product, O divided by the sum at the end.
  * scale <= 0 selects 1/sqrt(head_dim). head_dim must be 128, L % 8 == 0.
- * workspace: kvm_sm100_attention_workspace(B, L, HQ, HKV) bytes. */
+ * workspace: kvm_sm100_attention_workspace(B, L, HQ, HKV) bytes (0 in this
+ * build: the scores never leave the SM; workspace may then be NULL). */
 int64_t kvm_sm100_attention_workspace(int B, int L, int HQ, int HKV);
 int kvm_sm100_attention_prefill_bf16(const void* q, int64_t ldq, const void* k,
                                      int64_t ldk, const void* v, int64_t ldv,

@@ -48,20 +48,6 @@ struct GemmParams {
   float* topk_w;
   int top_k;
   int* status;           // device status word
-  // Batched, attention-shaped mode (bh_heads > 0): group g = b * bh_heads + h
-  // is an independent M x N x K product; its operands start at
-  //   A: row b*a_b_rows + h*a_h_rows,  column b*a_b_cols + h*a_h_cols
-  //   B: row b*b_b_rows + kh*b_h_rows, column b*b_b_cols + kh*b_h_cols,
-  //      kh = h / bh_group (grouped-query heads share a B head)
-  //   D: element b*d_b + h*d_h (row stride ldd).
-  // causal 1: skip tiles entirely above the diagonal (col0 > row0 + BM - 1);
-  // causal 2: stop the K loop at the diagonal (K_eff = min(K, row0 + BM)).
-  int bh_heads;
-  int bh_group;
-  int a_b_rows, a_h_rows, a_b_cols, a_h_cols;
-  int b_b_rows, b_h_rows, b_b_cols, b_h_cols;
-  long long d_b, d_h;
-  int causal;
 };
 
 // Where one output tile's operands and results live.
@@ -69,10 +55,7 @@ struct GemmTile {
   int row0, row_end, col0;  // rows [row0, row_end) valid; columns from col0
   int a_x, a_y;             // A box at K block kb: (a_x + kb*BK, a_y)
   int b_x, b_y;             // B: K-major (b_x + kb*BK, b_y); MN-major (b_x, b_y + kb*BK)
-  int kb_count;
-  long long d_base;         // element offset of the group's origin in D
   int g;
-  bool skip;
 };
 
 template <int BN>
@@ -195,21 +178,18 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
   const int G = p.num_groups;
-  const bool batched = p.bh_heads > 0;
   const int n_tiles = (p.N + BN - 1) / BN;
   const int k_blocks = (p.K + BK - 1) / BK;
-  const int m_tiles_b = (p.M + BM - 1) / BM;  // batched mode: per group
 
   // ---- setup: group table, barriers, TMEM
   if (threadIdx.x == 0) *abort_flag = 0;
-  if (!batched)
-    for (int i = threadIdx.x; i <= G; i += blockDim.x)
-      g_off[i] = p.offsets ? p.offsets[i] : (i == 0 ? 0 : p.M);
+  for (int i = threadIdx.x; i <= G; i += blockDim.x)
+    g_off[i] = p.offsets ? p.offsets[i] : (i == 0 ? 0 : p.M);
   __syncthreads();
   if (threadIdx.x == 0) {
     int acc = 0;
     bool bad = false;
-    for (int g = 0; g < (batched ? 0 : G); ++g) {
+    for (int g = 0; g < G; ++g) {
       int lo = g_off[g], hi = g_off[g + 1];
       if (lo < 0 || hi < lo || hi > p.M) {
         bad = true;
@@ -245,58 +225,28 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
-  const int total_tiles =
-      batched ? G * m_tiles_b * n_tiles : g_pref[G];
+  const int total_tiles = g_pref[G];
 
   auto map_tile = [&](int t) {
-    GemmTile tl;
-    tl.skip = false;
-    tl.kb_count = k_blocks;
-    if (!batched) {
-      int lo = 0, hi = G - 1;  // largest g with g_pref[g] <= t
-      while (lo < hi) {
-        int mid = (lo + hi + 1) >> 1;
-        if (g_pref[mid] <= t) lo = mid; else hi = mid - 1;
-      }
-      const int g = lo;
-      const int local = t - g_pref[g];
-      const int mt = g_mt[g];
-      const int nt = local / mt;
-      const int mi = local - nt * mt;
-      tl.g = g;
-      tl.row0 = g_off[g] + mi * BM;
-      tl.row_end = g_off[g + 1];
-      tl.col0 = nt * BN;
-      tl.a_x = 0;
-      tl.a_y = tl.row0;
-      tl.b_x = B_MN ? tl.col0 : 0;
-      tl.b_y = g * p.b_group_rows + (B_MN ? 0 : tl.col0);
-      tl.d_base = 0;
-    } else {
-      const int per = m_tiles_b * n_tiles;
-      const int g = t / per;
-      const int local = t - g * per;
-      const int nt = local / m_tiles_b;
-      const int mi = local - nt * m_tiles_b;
-      const int bi = g / p.bh_heads, hi = g - bi * p.bh_heads;
-      const int kh = hi / p.bh_group;
-      tl.g = g;
-      tl.row0 = mi * BM;
-      tl.row_end = p.M;
-      tl.col0 = nt * BN;
-      tl.a_x = bi * p.a_b_cols + hi * p.a_h_cols;
-      tl.a_y = bi * p.a_b_rows + hi * p.a_h_rows + tl.row0;
-      const int br = bi * p.b_b_rows + kh * p.b_h_rows;
-      const int bc = bi * p.b_b_cols + kh * p.b_h_cols;
-      tl.b_x = B_MN ? bc + tl.col0 : bc;
-      tl.b_y = B_MN ? br : br + tl.col0;
-      tl.d_base = bi * p.d_b + hi * p.d_h;
-      if (p.causal == 1) tl.skip = tl.col0 > tl.row0 + BM - 1;
-      if (p.causal == 2) {
-        const int k_eff = min(p.K, tl.row0 + BM);
-        tl.kb_count = (k_eff + BK - 1) / BK;
-      }
+    int lo = 0, hi = G - 1;  // largest g with g_pref[g] <= t
+    while (lo < hi) {
+      int mid = (lo + hi + 1) >> 1;
+      if (g_pref[mid] <= t) lo = mid; else hi = mid - 1;
     }
+    const int g = lo;
+    const int local = t - g_pref[g];
+    const int mt = g_mt[g];
+    const int nt = local / mt;
+    const int mi = local - nt * mt;
+    GemmTile tl;
+    tl.g = g;
+    tl.row0 = g_off[g] + mi * BM;
+    tl.row_end = g_off[g + 1];
+    tl.col0 = nt * BN;
+    tl.a_x = 0;
+    tl.a_y = tl.row0;
+    tl.b_x = B_MN ? tl.col0 : 0;
+    tl.b_y = g * p.b_group_rows + (B_MN ? 0 : tl.col0);
     return tl;
   };
 
@@ -312,8 +262,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       bool ok = true;
       for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
         const GemmTile tl = map_tile(t);
-        if (tl.skip) continue;
-        for (int kb = 0; kb < tl.kb_count; ++kb) {
+        for (int kb = 0; kb < k_blocks; ++kb) {
           if (!mbar_wait(&empty[s], ph ^ 1, abort_flag)) { ok = false; break; }
           uint8_t* a_dst = smem + s * S::kStageBytes;
           uint8_t* b_dst = a_dst + S::kABytes;
@@ -347,15 +296,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       int it = 0;
       bool ok = true;
       for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
-        const GemmTile tl = map_tile(t);
-        if (tl.skip) continue;
         const int acc = it & 1;
         const uint32_t aph = (it >> 1) & 1;
         ++it;
         if (!mbar_wait(&tempty[acc], aph ^ 1, abort_flag)) { ok = false; break; }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * BN;
-        for (int kb = 0; kb < tl.kb_count; ++kb) {
+        for (int kb = 0; kb < k_blocks; ++kb) {
           if (!mbar_wait(&full[s], ph, abort_flag)) { ok = false; break; }
           tc_fence_after();
           const uint32_t a_addr = smem_u32(smem + s * S::kStageBytes);
@@ -385,7 +332,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     int it = 0;
     for (int t = blockIdx.x; t < total_tiles; t += gridDim.x) {
       const GemmTile tl = map_tile(t);
-      if (tl.skip) continue;
       const int row0 = tl.row0, row_end = tl.row_end, col0 = tl.col0;
       const int acc = it & 1;
       const uint32_t aph = (it >> 1) & 1;
@@ -413,7 +359,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 #pragma unroll
             for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
             char* dst = static_cast<char*>(p.D) +
-                        (tl.d_base + static_cast<long long>(row) * p.ldd + col) * ES;
+                        (static_cast<long long>(row) * p.ldd + col) * ES;
             const char* crow =
                 p.C ? static_cast<const char*>(p.C) +
                           (static_cast<long long>(row) * p.ldc + col) * ES

@@ -70,11 +70,9 @@ class TPDecoderLayer:
                    batch=batch, seq_len=seq_len, heads_q=heads_q, heads_kv=heads_kv,
                    rank=rank, world=world, group=group)
 
-    # kernels of our own per call: 2 RMSNorm, 4 GEMM, 2 RoPE, attention
-    # (3 launches per chunk of heads and batch element)
+    # kernels of our own per call: 2 RMSNorm, 4 GEMM, 2 RoPE, 1 fused attention
     def launches(self) -> int:
-        chunks = self.B * -(-self.hq // max(1, min(self.hq, 16)))
-        return 8 + 3 * chunks
+        return 9
 
     def __call__(self, x: torch.Tensor, probe=None) -> torch.Tensor:
         hq, hkv, L = self.hq, self.hkv, self.L

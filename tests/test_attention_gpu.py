@@ -61,3 +61,23 @@ def test_rope(cuda, rows, L, heads):
     g, r = oracle.bf16_to_f32(got[:, :heads * 128]), oracle.bf16_to_f32(ref)
     assert rel_err(g, r) < 1e-2
     assert np.mean(got[:, :heads * 128] != ref) < 0.01   # at most rare 1-ulp flips
+
+
+def test_attention_rescales_when_later_keys_dominate(cuda):
+    """Keys of a later tile with 8x the scale raise each row's running max by
+    far more than 2^8, so the fused kernel rescales its TMEM accumulator."""
+    rng = np.random.default_rng(11)
+    B, L, HQ, HKV, hd = 1, 512, 2, 1, 128
+    q = oracle.normal_bf16(rng, (B * L, HQ * hd))
+    kf = oracle.bf16_to_f32(oracle.normal_bf16(rng, (B * L, HKV * hd)))
+    kf[384:512] *= 8.0
+    kf[200:210] *= 4.0
+    k = oracle.f32_to_bf16(kf)
+    v = oracle.normal_bf16(rng, (B * L, HKV * hd))
+    ref = oracle.attention(q, k, v, B, HQ, HKV)
+    out = ops.attention_prefill(from_bits(q, cuda), from_bits(k, cuda), from_bits(v, cuda),
+                                batch=B, heads_q=HQ, heads_kv=HKV)
+    ops.device_status()
+    got = oracle.bf16_to_f32(to_bits(out))
+    assert np.isfinite(got).all()
+    assert rel_err(got, oracle.bf16_to_f32(ref)) < 1e-2
