@@ -246,9 +246,9 @@ static int grouped_impl(const void* A, long long lda, const void* B, void* D,
     return launch_pair<kEpiBf16>(maps, pp, ub, st);
   }
 
-  // One-SM kernel: SiLU-gate tiles of 128 columns hold one 64-row gate block
-  // and its up block.
-  const int BN = epilogue == kEpiSilu ? 128 : 256;
+  // One-SM kernel, 128 x 256 tiles (two 64-row gate blocks and their up
+  // blocks for SiLU-gate).
+  constexpr int BN = 256;
   const long long ub = (long long)(cdiv(rows, kGemmBM) + G) * cdiv(N, BN);
   const int grid = ub < dev->sm_count ? int(ub) : dev->sm_count;
   CUtensorMap ta, tb;
@@ -259,8 +259,8 @@ static int grouped_impl(const void* A, long long lda, const void* B, void* D,
                          BN, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
                          CU_TENSOR_MAP_SWIZZLE_128B));
   if (epilogue == kEpiSilu)
-    return launch<128, 6, false, kEpiSilu>(ta, tb, p, grid, st);
-  return launch<256, 4, false, kEpiBf16>(ta, tb, p, grid, st);
+    return launch<BN, 4, false, kEpiSilu>(ta, tb, p, grid, st);
+  return launch<BN, 4, false, kEpiBf16>(ta, tb, p, grid, st);
 }
 
 extern "C" int kvm_sm100_gemm_bf16_silu_gate(const void* A, int64_t lda,

@@ -23,7 +23,8 @@ namespace kvm {
 enum GemmEpilogue : int {
   kEpiBf16 = 0,    // D = bf16(acc [+ C])
   kEpiF32 = 1,     // D = acc [+ C] (fp32)
-  kEpiSilu = 2,    // tile cols [0,BN/2) gate, [BN/2,BN) up -> bf16 SiLU(g)*u
+  kEpiSilu = 2,    // per 128 tile cols: 64 gate, then the 64 up of the same
+                   // f (pack_gate_up layout) -> bf16 SiLU(g)*u
   kEpiRouter = 3,  // BN = 64 >= E: logits + softmax + top-k per row
 };
 
@@ -371,8 +372,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 #pragma unroll 1
         for (int c = 0; c < BN / 64; ++c) {
           uint32_t rg[32], ru[32];
-          tmem_ld32(t_row + c * 32, rg);
-          tmem_ld32(t_row + BN / 2 + c * 32, ru);
+          const int gcol = (c >> 1) * 128 + (c & 1) * 32;  // gate; up is 64 on
+          tmem_ld32(t_row + gcol, rg);
+          tmem_ld32(t_row + gcol + 64, ru);
           tmem_wait_ld();
           const int col = col0 / 2 + c * 32;  // output column
           if (row_ok && col < p.N / 2) {

@@ -25,7 +25,12 @@
 // Splitting them into exact boxes (64 + 8 for 72 rows) costs more TMA time
 // than the extra rows, and L2 prefetch of the weights ahead of the TMA loads
 // (bulk tensor prefetch or prefetch.global.L2 from a spare warp) made the
-// weight stream slower, not faster, on B200.
+// weight stream slower, not faster, on B200. So did "wide" tiles of up to
+// 512 tokens (two MMAs per K block sharing one weight stage, the second
+// group of tokens in a second stage): they halve the weight bytes in flight
+// per SM, and the weight stream from HBM is what bounds this kernel (a group
+// of 512 tokens: 663 us as one wide tile vs 587 us as two narrow tiles whose
+// second weight read hits L2).
 //
 // Epilogues: plain (bf16 D [+ C]) and SiLU-gate. For SiLU-gate the weight
 // rows come from pack_gate_up (64-row blocks: gate f0..f0+63, then up
