@@ -304,6 +304,67 @@ int kvm_sm100_attention_prefill_bf16(const void* q, int64_t ldq, const void* k,
                                      void* workspace, int64_t workspace_bytes,
                                      kvm_stream_t stream);
 
+/* ------------------------------------------------- paged KV cache --- */
+
+/* A paged K/V pool as KVMeta describes it (src/ir/graph_config.h:20-39):
+ * pages of block_size token slots; a slot holds `width` = layer_size
+ * elements (HKV heads x head_dim, bf16) of K or of V for one layer. Element
+ * (page, layer, kv, slot, e) lives at
+ *   page*page_stride + layer*layer_stride + kv*kv_stride + slot*token_stride + e
+ * (kv 0 = K, 1 = V), which covers layout=page_first
+ * ([page][layer][kv][slot][width]) and layer_first ([layer][page][kv]...).
+ * No counterpart struct in the reference: it carries KVMeta's fields plus
+ * the strides they imply. */
+typedef struct kvm_kv_layout {
+  int64_t page_stride;
+  int64_t layer_stride;
+  int64_t kv_stride;
+  int64_t token_stride;
+  int32_t block_size;
+  int32_t layer;      /* the layer this call reads or writes */
+  int32_t width;      /* elements per slot: HKV * head_dim */
+  int32_t num_pages;  /* pages in the pool (page ids are checked) */
+} kvm_kv_layout;
+
+/* kernel.kvcache.write (src/ir/dialect/kernel/dialect.cpp:70): S sequences;
+ * the new rows q_offsets[s]..q_offsets[s+1] of k and v ([rows, width], row
+ * strides ldk/ldv) sit at positions q_positions[s] + i and go to slot
+ * pos % block_size of page block_table[bt_offsets[s] + pos / block_size].
+ * Page ids outside [0, num_pages) are reported through the device status
+ * and not written. */
+int kvm_sm100_kvcache_write(void* cache, const kvm_kv_layout* layout, const void* k,
+                            int64_t ldk, const void* v, int64_t ldv,
+                            const int32_t* q_offsets, const int32_t* q_positions,
+                            const int32_t* block_table, const int32_t* bt_offsets, int S,
+                            int rows, kvm_stream_t stream);
+
+/* kernel.kvcache.read (dialect.cpp:69): the first kv_offsets[s+1] -
+ * kv_offsets[s] cached tokens of each sequence gathered in order into rows
+ * kv_offsets[s].. of k and v ([rows, width], contiguous). */
+int kvm_sm100_kvcache_read(const void* cache, const kvm_kv_layout* layout, void* k,
+                           void* v, const int32_t* kv_offsets, const int32_t* block_table,
+                           const int32_t* bt_offsets, int S, int rows, kvm_stream_t stream);
+
+/* kernel.attn.decode (dialect.cpp:39) over the paged cache, causal: query
+ * row r of sequence s (rows q_offsets[s]..) at position p = q_positions[s]
+ * + (r - q_offsets[s]) attends to cached positions 0..p of s (written
+ * before the call); q and out are [rows, HQ*128] (row strides ldq, ldo), q
+ * head h reads kv head h / (HQ/HKV), HKV = width / 128, at most 32 query
+ * heads per kv head, block_size a power of two >= 16. The keys are split in
+ * chunks of 1024 over the SMs and merged; max_q_rows bounds the new rows of
+ * any sequence and max_keys the keys any row attends to (both size the
+ * workspace: kvm_sm100_attention_decode_workspace bytes). scale <= 0 selects
+ * 1/sqrt(128). */
+int64_t kvm_sm100_attention_decode_workspace(int S, int HQ, int HKV, int max_q_rows,
+                                             int max_keys);
+int kvm_sm100_attention_decode_paged(const void* q, int64_t ldq, const void* cache,
+                                     const kvm_kv_layout* layout, void* out, int64_t ldo,
+                                     const int32_t* q_offsets, const int32_t* q_positions,
+                                     const int32_t* block_table, const int32_t* bt_offsets,
+                                     int S, int HQ, int max_q_rows, int max_keys,
+                                     float scale, void* workspace, int64_t workspace_bytes,
+                                     kvm_stream_t stream);
+
 /* Rotary position embedding in place, rotate-half form: kernel.attn.rope
  * (dialect.cpp:40). Rows are tokens b*L + pos (row stride ld elements); heads
  * are consecutive head_dim-wide column blocks; for i < head_dim/2,

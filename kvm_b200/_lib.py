@@ -89,6 +89,11 @@ SIGNATURES = {
     "kvm_sm100_fill_normal": (_I, [_P, _I, _I64, C.c_uint64, _F, _F, _P]),
     "kvm_sm100_rmsnorm_bf16": (_I, [_P, _P, _P, _I, _I, _F, _P]),
     "kvm_sm100_silu_mul_bf16": (_I, [_P, _P, _P, _I64, _P]),
+    "kvm_sm100_kvcache_write": (_I, [_P, _P, _P, _I64, _P, _I64, _P, _P, _P, _P, _I, _I, _P]),
+    "kvm_sm100_kvcache_read": (_I, [_P, _P, _P, _P, _P, _P, _P, _I, _I, _P]),
+    "kvm_sm100_attention_decode_workspace": (_I64, [_I, _I, _I, _I, _I]),
+    "kvm_sm100_attention_decode_paged": (_I, [_P, _I64, _P, _P, _P, _I64, _P, _P, _P, _P,
+                                              _I, _I, _I, _I, _F, _P, _I64, _P]),
 }
 
 KVM_EP_MAX_RANKS = 8
@@ -101,6 +106,14 @@ class EpPeers(C.Structure):
                 ("recv", C.c_void_p * KVM_EP_MAX_RANKS), ("y", C.c_void_p * KVM_EP_MAX_RANKS),
                 ("cnt", C.c_void_p * KVM_EP_MAX_RANKS),
                 ("flags", C.c_void_p * KVM_EP_MAX_RANKS)]
+
+
+class KvLayout(C.Structure):
+    """Mirror of struct kvm_kv_layout (include/kvm_sm100.h)."""
+    _fields_ = [("page_stride", C.c_int64), ("layer_stride", C.c_int64),
+                ("kv_stride", C.c_int64), ("token_stride", C.c_int64),
+                ("block_size", C.c_int32), ("layer", C.c_int32), ("width", C.c_int32),
+                ("num_pages", C.c_int32)]
 
 
 _lib: C.CDLL | None = None

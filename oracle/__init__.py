@@ -62,6 +62,11 @@ def lib() -> C.CDLL:
         L.orc_gemm_fp8_blockscaled.argtypes = [P, P, P, P, P, I, I, I]
         L.orc_rope_bf16.argtypes = [P, I64, I, I, I, I, F]
         L.orc_attention_bf16.argtypes = [P, I64, P, I64, P, I64, P, I64, I, I, I, I, I, F]
+        L.orc_kvcache_write.argtypes = [P, I64, I64, I64, I64, I, I, I, P, I64, P, I64,
+                                        P, P, P, P, I]
+        L.orc_kvcache_read.argtypes = [P, I64, I64, I64, I64, I, I, I, P, P, P, P, P, I]
+        L.orc_attention_decode.argtypes = [P, I64, P, I64, I64, I64, I64, I, I, P, I64,
+                                           P, P, P, P, I, I, I, I, F]
         _lib = L
     return _lib
 
@@ -262,6 +267,68 @@ def attention(q, k, v, B: int, HQ: int, HKV: int, hd: int = 128, scale: float = 
     out = np.empty((q.shape[0], HQ * hd), dtype=np.uint16)
     lib().orc_attention_bf16(_p(q), q.shape[1], _p(k), k.shape[1], _p(v), v.shape[1],
                              _p(out), out.shape[1], B, L, HQ, HKV, hd, float(scale))
+    return out
+
+
+# ------------------------------------------------------- paged KV cache ---
+
+def kv_strides(layout: str, pages: int, layers: int, block_size: int, width: int):
+    """Element strides (page, layer, kv, token) of a paged KV pool holding K
+    and V for `layers` layers: page_first = [page][layer][kv][slot][width],
+    layer_first = [layer][page][kv][slot][width]."""
+    tok = width
+    kv = block_size * width
+    if layout == "page_first":
+        layer = 2 * kv
+        page = layers * layer
+    elif layout == "layer_first":
+        page = 2 * kv
+        layer = pages * page
+    else:
+        raise ValueError(layout)
+    return page, layer, kv, tok
+
+
+def _i32(a) -> np.ndarray:
+    return np.ascontiguousarray(np.asarray(a, dtype=np.int32))
+
+
+def kvcache_write(cache: np.ndarray, strides, block_size: int, layer: int, k, v,
+                  q_off, q_pos, bt, bt_off) -> np.ndarray:
+    """Copy of the flat bf16 pool `cache` with the new tokens' K/V rows written."""
+    cache = np.array(_c(cache, np.uint16), copy=True)
+    k, v = _c(k, np.uint16), _c(v, np.uint16)
+    q_off, q_pos, bt, bt_off = _i32(q_off), _i32(q_pos), _i32(bt), _i32(bt_off)
+    lib().orc_kvcache_write(_p(cache), *strides, block_size, layer, k.shape[1], _p(k),
+                            k.shape[1], _p(v), v.shape[1], _p(q_off), _p(q_pos), _p(bt),
+                            _p(bt_off), len(q_off) - 1)
+    return cache
+
+
+def kvcache_read(cache: np.ndarray, strides, block_size: int, layer: int, width: int,
+                 kv_off, bt, bt_off):
+    """(k, v) [sum kv_len, width]: each sequence's cached tokens in order."""
+    cache = _c(cache, np.uint16)
+    kv_off, bt, bt_off = _i32(kv_off), _i32(bt), _i32(bt_off)
+    rows = int(kv_off[-1])
+    k = np.empty((rows, width), dtype=np.uint16)
+    v = np.empty((rows, width), dtype=np.uint16)
+    lib().orc_kvcache_read(_p(cache), *strides, block_size, layer, width, _p(k), _p(v),
+                           _p(kv_off), _p(bt), _p(bt_off), len(kv_off) - 1)
+    return k, v
+
+
+def attention_decode(q, cache, strides, block_size: int, layer: int, q_off, q_pos, bt,
+                     bt_off, HQ: int, HKV: int, hd: int = 128, scale: float = 0.0):
+    """Causal attention of the new query rows over the paged cache."""
+    q, cache = _c(q, np.uint16), _c(cache, np.uint16)
+    q_off, q_pos, bt, bt_off = _i32(q_off), _i32(q_pos), _i32(bt), _i32(bt_off)
+    if scale <= 0:
+        scale = 1.0 / np.sqrt(hd)
+    out = np.empty((q.shape[0], HQ * hd), dtype=np.uint16)
+    lib().orc_attention_decode(_p(q), q.shape[1], _p(cache), *strides, block_size, layer,
+                               _p(out), out.shape[1], _p(q_off), _p(q_pos), _p(bt),
+                               _p(bt_off), len(q_off) - 1, HQ, HKV, hd, float(scale))
     return out
 
 

@@ -518,3 +518,109 @@ void orc_attention_bf16(const uint16_t* q, int64_t ldq, const uint16_t* k,
       free(pf);
     }
 }
+
+/* ---------------------------------------------------- paged KV cache --- */
+
+/* Element offset of (page, kv, slot) in a paged cache: kv 0 = K, 1 = V. The
+ * strides (elements) describe either KVMeta layout (src/ir/graph_config.h:
+ * 20-39): page_first = [page][layer][kv][slot][layer_size], layer_first =
+ * [layer][page][kv][slot][layer_size]. */
+static int64_t kv_at(int64_t page_stride, int64_t layer_stride, int64_t kv_stride,
+                     int64_t token_stride, int layer, int page, int kv, int slot) {
+  return (int64_t)page * page_stride + (int64_t)layer * layer_stride +
+         (int64_t)kv * kv_stride + (int64_t)slot * token_stride;
+}
+
+/* kernel.kvcache.write (src/ir/dialect/kernel/dialect.cpp:70): the new
+ * tokens' K and V rows (rows q_off[s]..q_off[s+1] of sequence s, positions
+ * q_pos[s] + i) go to slot pos % bs of page bt[bt_off[s] + pos / bs]. */
+void orc_kvcache_write(uint16_t* cache, int64_t page_stride, int64_t layer_stride,
+                       int64_t kv_stride, int64_t token_stride, int bs, int layer,
+                       int width, const uint16_t* k, int64_t ldk, const uint16_t* v,
+                       int64_t ldv, const int32_t* q_off, const int32_t* q_pos,
+                       const int32_t* bt, const int32_t* bt_off, int S) {
+  for (int s = 0; s < S; ++s)
+    for (int r = q_off[s]; r < q_off[s + 1]; ++r) {
+      const int pos = q_pos[s] + (r - q_off[s]);
+      const int page = bt[bt_off[s] + pos / bs], slot = pos % bs;
+      memcpy(cache + kv_at(page_stride, layer_stride, kv_stride, token_stride, layer,
+                           page, 0, slot),
+             k + (int64_t)r * ldk, sizeof(uint16_t) * (size_t)width);
+      memcpy(cache + kv_at(page_stride, layer_stride, kv_stride, token_stride, layer,
+                           page, 1, slot),
+             v + (int64_t)r * ldv, sizeof(uint16_t) * (size_t)width);
+    }
+}
+
+/* kernel.kvcache.read (dialect.cpp:69): the first kv_len[s] cached tokens of
+ * each sequence, gathered into rows kv_off[s].. of k and v ([rows, width]). */
+void orc_kvcache_read(const uint16_t* cache, int64_t page_stride, int64_t layer_stride,
+                      int64_t kv_stride, int64_t token_stride, int bs, int layer,
+                      int width, uint16_t* k, uint16_t* v, const int32_t* kv_off,
+                      const int32_t* bt, const int32_t* bt_off, int S) {
+  for (int s = 0; s < S; ++s)
+    for (int j = 0; j < kv_off[s + 1] - kv_off[s]; ++j) {
+      const int page = bt[bt_off[s] + j / bs], slot = j % bs;
+      const int64_t r = kv_off[s] + j;
+      memcpy(k + r * width,
+             cache + kv_at(page_stride, layer_stride, kv_stride, token_stride, layer,
+                           page, 0, slot),
+             sizeof(uint16_t) * (size_t)width);
+      memcpy(v + r * width,
+             cache + kv_at(page_stride, layer_stride, kv_stride, token_stride, layer,
+                           page, 1, slot),
+             sizeof(uint16_t) * (size_t)width);
+    }
+}
+
+/* kernel.attn.decode (dialect.cpp:39) over the paged cache: query row r of
+ * sequence s sits at position p = q_pos[s] + (r - q_off[s]) and attends to
+ * the cached positions 0..p of s (GQA: q head h reads kv head h / (HQ/HKV)).
+ * s_j = dot(q, k_j) (16-lane order), m = max(scale*s), l = sum exp(scale*s_j
+ * - m) (index order), out = bf16(sum_j exp(scale*s_j - m) v_j / l) (fp32,
+ * 16-lane order over j). */
+void orc_attention_decode(const uint16_t* q, int64_t ldq, const uint16_t* cache,
+                          int64_t page_stride, int64_t layer_stride, int64_t kv_stride,
+                          int64_t token_stride, int bs, int layer, uint16_t* out,
+                          int64_t ldo, const int32_t* q_off, const int32_t* q_pos,
+                          const int32_t* bt, const int32_t* bt_off, int S, int HQ,
+                          int HKV, int hd, float scale) {
+  const int group = HQ / HKV;
+  for (int s = 0; s < S; ++s) {
+    const int n = q_off[s + 1] - q_off[s];
+#pragma omp parallel for collapse(2) schedule(dynamic, 1)
+    for (int i = 0; i < n; ++i)
+      for (int h = 0; h < HQ; ++h) {
+        const int64_t r = q_off[s] + i;
+        const int pos = q_pos[s] + i, kh = h / group;
+        float* qf = (float*)malloc(sizeof(float) * (size_t)hd);
+        float* e = (float*)malloc(sizeof(float) * (size_t)(pos + 1));
+        for (int d = 0; d < hd; ++d) qf[d] = bf2f(q[r * ldq + (int64_t)h * hd + d]);
+        float m = -INFINITY;
+        for (int j = 0; j <= pos; ++j) {
+          const uint16_t* kr =
+              cache + kv_at(page_stride, layer_stride, kv_stride, token_stride, layer,
+                            bt[bt_off[s] + j / bs], 0, j % bs) + (int64_t)kh * hd;
+          e[j] = dot_f32_bf16(qf, kr, hd) * scale;
+          m = fmaxf(m, e[j]);
+        }
+        float l = 0.0f;
+        for (int j = 0; j <= pos; ++j) {
+          e[j] = expf(e[j] - m);
+          l += e[j];
+        }
+        for (int d = 0; d < hd; ++d) {
+          float lanes[LANES] = {0};
+          for (int j = 0; j <= pos; ++j) {
+            const uint16_t* vr =
+                cache + kv_at(page_stride, layer_stride, kv_stride, token_stride, layer,
+                              bt[bt_off[s] + j / bs], 1, j % bs) + (int64_t)kh * hd;
+            lanes[j % LANES] += e[j] * bf2f(vr[d]);
+          }
+          out[r * ldo + (int64_t)h * hd + d] = f2bf(lanes_sum(lanes) / l);
+        }
+        free(qf);
+        free(e);
+      }
+  }
+}

@@ -181,3 +181,27 @@ def test_rope_oracle_matches_float64():
             ref[r, h * hd:h * hd + hd // 2] = a * np.cos(th) - b * np.sin(th)
             ref[r, h * hd + hd // 2:(h + 1) * hd] = b * np.cos(th) + a * np.sin(th)
     assert rel_err(got, ref) < 4e-3
+
+
+def test_paged_kv_oracle_matches_dense_attention():
+    """Writing a sequence into shuffled pages, reading it back and decoding
+    every row over the pages equals the dense causal attention oracle."""
+    rng = np.random.default_rng(9)
+    HKV, HQ, L, bs, pages, layers = 2, 4, 70, 16, 12, 2
+    W = HKV * 128
+    for layout in ("page_first", "layer_first"):
+        st = oracle.kv_strides(layout, pages, layers, bs, W)
+        pool = np.zeros(pages * layers * 2 * bs * W, dtype=np.uint16)
+        bt = rng.permutation(pages)[:5].astype(np.int32)
+        k = oracle.normal_bf16(rng, (L, W))
+        v = oracle.normal_bf16(rng, (L, W))
+        q = oracle.normal_bf16(rng, (L, HQ * 128))
+        pool = oracle.kvcache_write(pool, st, bs, 1, k, v, [0, L], [0], bt, [0, 5])
+        kr, vr = oracle.kvcache_read(pool, st, bs, 1, W, [0, L], bt, [0, 5])
+        assert np.array_equal(kr, k) and np.array_equal(vr, v)
+        out = oracle.attention_decode(q, pool, st, bs, 1, [0, L], [0], bt, [0, 5], HQ, HKV)
+        ref = oracle.attention(q, k, v, 1, HQ, HKV)
+        assert rel_err(oracle.bf16_to_f32(out), oracle.bf16_to_f32(ref)) < 1e-2
+        # layer 0 untouched
+        other = oracle.kvcache_read(pool, st, bs, 0, W, [0, L], bt, [0, 5])[0]
+        assert not other.any()
