@@ -10,6 +10,11 @@ bench.py's format.
         352 MB of weights per step (> L2).
   fp8   W8A8 block-scaled GEMM [M,8192] x [8192,28672] e4m3 with 128x128 fp32
         scales, bf16 out, M in {16, 128, 1024}; 235 MB of weights (> L2).
+  decode  one decode step of 64 sequences over a paged KV cache: 4096 cached
+        tokens each, 64 query / 8 kv heads of 128 (the decoder layer's heads),
+        16-token pages scattered over the pool (page_first); a step writes
+        the new token's K/V (kvcache.write) and runs attn.decode over the
+        4097 keys. 1.07 GB of K/V read per step (> L2).
 Data: seeded torch.randn on the device, weights N(0, 0.02) (fp8: N(0,1)
 quantised per block to amax 448).
 """
@@ -154,6 +159,52 @@ def run_tp(args, peaks, ClockSampler) -> int:
     return 0
 
 
+def run_decode(args, peaks, ClockSampler, dev, g) -> int:
+    from .kvcache import PagedKVCache
+    S, ctx, HQ, HKV, bs = 64, 4096, 64, 8, 16
+    keys = ctx + 1
+    per_seq = (keys + bs - 1) // bs
+    pages = S * per_seq
+    cache = PagedKVCache(pages=pages, layers=1, block_size=bs, heads_kv=HKV,
+                         layout="page_first", device=dev)
+    cache.pool.copy_(torch.randn(cache.pool.shape, generator=g, device=dev))
+    perm = torch.randperm(pages, generator=g, device=dev).to(torch.int32)
+    bt_off = (torch.arange(S + 1, device=dev, dtype=torch.int32) * per_seq)
+    q_off = torch.arange(S + 1, device=dev, dtype=torch.int32)
+    q_pos = torch.full((S,), ctx, device=dev, dtype=torch.int32)
+    q = torch.randn((S, HQ * 128), generator=g, device=dev).to(torch.bfloat16)
+    k = torch.randn((S, HKV * 128), generator=g, device=dev).to(torch.bfloat16)
+    v = torch.randn((S, HKV * 128), generator=g, device=dev).to(torch.bfloat16)
+    out = torch.empty((S, HQ * 128), dtype=torch.bfloat16, device=dev)
+    from ._lib import lib
+    ws = torch.empty(int(lib().kvm_sm100_attention_decode_workspace(S, HQ, HKV, 1, keys)),
+                     dtype=torch.uint8, device=dev)
+    steps, warmup = args.steps, max(args.warmup, 3)
+
+    def step():
+        cache.write(0, k, v, q_off, q_pos, perm, bt_off)
+        cache.decode(0, q, q_off, q_pos, perm, bt_off, heads_q=HQ, max_q_rows=1,
+                     max_keys=keys, out=out, workspace=ws)
+    with ClockSampler(0) as ck:
+        t0 = time.time()
+        ms = _time(step, steps, warmup)
+        t1 = time.time()
+    kv_bytes = S * HKV * keys * 128 * 2 * 2
+    byt = kv_bytes + 2 * S * HQ * 128 * 2 + 2 * S * HKV * 128 * 2
+    gbs = byt / (ms / 1e3) / 1e9
+    flop = 4.0 * S * HQ * keys * 128
+    _line(args, ck, t0, t1, metric="paged decode attention GB/s", value=gbs, unit="GB/s",
+          ms_per_step=ms, dtype="bf16",
+          config={"workload": "paged_decode_S64_ctx4096_HQ64_HKV8_hd128_bs16",
+                  "kv_bytes_per_step": kv_bytes, "tflops": flop / (ms / 1e3) / 1e12,
+                  "l2": "1.07 GB of K/V per step > L2"},
+          roofline={"bound": "hbm", "achieved": gbs, "peak": peaks["hbm"], "unit": "GB/s",
+                    "frac": gbs / peaks["hbm"], "traffic": None,
+                    "kernel": "decode_attn_kernel + combine + kvcache.write"},
+          gpu_launches=3 * steps)
+    return 0
+
+
 def run(args, peaks, ClockSampler) -> int:
     if args.workload == "tp":
         return run_tp(args, peaks, ClockSampler)
@@ -181,6 +232,8 @@ def run(args, peaks, ClockSampler) -> int:
                         "unit": "TFLOP/s", "frac": tf / peaks["bf16"], "traffic": None},
               gpu_launches=steps)
         return 0
+    if args.workload == "decode":
+        return run_decode(args, peaks, ClockSampler, dev, g)
     if args.workload == "mlp":
         T, H, F = 4096, 4096, 14336
         x = torch.randn((T, H), generator=g, device=dev).to(torch.bfloat16)

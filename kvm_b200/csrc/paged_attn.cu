@@ -16,8 +16,11 @@
 // K and V pages land in shared memory by TMA straight from the page table
 // (one box per page half), so the cache is never gathered in HBM.
 //
-//   warp 0 (one lane)  TMA producer: K/V tiles of 128 keys, 3-stage ring
-//   warp 1 (one lane)  MMA issuer: S_j, then (after P_j) PV_j
+//   warp 0             TMA producer: the warp reads an item's page ids into
+//                      shared memory, then per 128-key tile one lane per
+//                      page issues its K and V boxes into two 3-stage rings
+//   warp 1 (one lane)  MMA issuer: S_0, then S_{j+1} before PV_j (S and P
+//                      double-buffered), so softmax j overlaps the next S
 //   warps 2..5         thread = key (S^T lanes) and = head dim (O^T lanes):
 //                      causal mask, per-column max by a warp transpose
 //                      reduction + one shared-memory exchange per tile,
@@ -41,19 +44,33 @@ namespace {
 
 constexpr int kDecThreads = 192;
 constexpr int kDecMaxN = 32;           // query rows x heads per item
-constexpr int kDecStages = 3;
-constexpr int kDecChunk = 1024;        // keys per item
-constexpr uint32_t kDecHalf = 128 * 64 * 2;   // 128 keys x 64 dims: 16 KB
-constexpr uint32_t kDecStageBytes = 4 * kDecHalf;  // K and V tiles: 64 KB
-constexpr uint32_t kDecOffQ = kDecStages * kDecStageBytes;
-constexpr uint32_t kDecQBytes = 2 * kDecMaxN * 128;   // 2 atoms x 32 rows
-constexpr uint32_t kDecOffP = kDecOffQ + kDecQBytes;
-constexpr uint32_t kDecOffRed = kDecOffP + kDecQBytes;  // [2][4][32] floats
-constexpr uint32_t kDecOffBar = kDecOffRed + 2 * 4 * 32 * 4;
-constexpr int kDecBars = 2 * kDecStages + 10;
+constexpr int kDecStages = 3;          // K ring and V ring, 3 tiles each
+constexpr int kDecChunk = 1024;        // at most this many keys per item
+constexpr uint32_t kDecHalf = 128 * 64 * 2;    // 128 keys x 64 dims: 16 KB
+constexpr uint32_t kDecTile = 2 * kDecHalf;    // 128 keys x 128 dims: 32 KB
+constexpr uint32_t kDecOffK = 0;
+constexpr uint32_t kDecOffV = kDecStages * kDecTile;
+constexpr uint32_t kDecOffQ = 2 * kDecStages * kDecTile;
+constexpr uint32_t kDecQBytes = 2 * kDecMaxN * 128;   // 2 atoms x 32 rows: 8 KB
+constexpr uint32_t kDecOffP = kDecOffQ + kDecQBytes;  // [2] P^T buffers
+constexpr uint32_t kDecOffRed = kDecOffP + 2 * kDecQBytes;  // [2][4][32] floats
+constexpr uint32_t kDecOffPages = kDecOffRed + 2 * 4 * 32 * 4;  // page ids of an item
+constexpr int kDecMaxPages = kDecChunk / 16 + 1;
+constexpr uint32_t kDecOffBar = kDecOffPages + ((kDecMaxPages * 4 + 15) & ~15);
+constexpr int kDecBars = 4 * kDecStages + 15;  // == kBarCount
 constexpr float kDecRescale = 8.0f;
 
 constexpr size_t dec_smem_bytes() { return 1024 + kDecOffBar + kDecBars * 8 + 16; }
+
+// Keys of a group are split into nch = ceil(need / 1024) chunks of equal
+// size (a multiple of 128): chunk c covers [c * size, min((c+1) * size, need)).
+__host__ __device__ __forceinline__ int dec_chunks(int need) {
+  return (need + kDecChunk - 1) / kDecChunk;
+}
+__host__ __device__ __forceinline__ int dec_chunk_size(int need) {
+  const int n = dec_chunks(need);
+  return n ? (((need + n - 1) / n + 127) & ~127) : 0;
+}
 
 struct DecParams {
   const __nv_bfloat16* q;
@@ -95,17 +112,28 @@ __device__ __forceinline__ DecItem dec_item(const DecParams& p, int w) {
   it.nq = min(p.nqg, q1 - it.r_begin);
   it.pos0 = p.q_pos[it.s] + (it.r_begin - q0);
   it.need = it.nq > 0 ? it.pos0 + it.nq : 0;
-  it.t_begin = it.c * kDecChunk;
-  it.t_end = min(it.t_begin + kDecChunk, it.need);
+  const int csz = dec_chunk_size(it.need);
+  it.t_begin = it.c < dec_chunks(it.need) ? it.c * csz : it.need;
+  it.t_end = min(it.t_begin + csz, it.need);
   return it;
 }
 
-// Warp transpose reduction: lane l ends with the reduction over all lanes of
-// column l of v[32] (31 shuffles).
-template <bool MAX>
-__device__ __forceinline__ float warp_columns(float (&v)[32], int lane) {
+// Column reduction over a warp: v[NC] holds this lane's values of NC
+// columns; on return lane l holds the reduction over all 32 lanes of column
+// l % NC (fold the lanes that carry the same columns, then a transpose
+// reduction: 31 shuffles for NC = 32 or 16).
+template <int NC, bool MAX>
+__device__ __forceinline__ float warp_columns(float (&v)[NC], int lane) {
 #pragma unroll
-  for (int o = 16; o >= 1; o >>= 1) {
+  for (int o = 16; o >= NC; o >>= 1) {
+#pragma unroll
+    for (int i = 0; i < NC; ++i) {
+      const float r = __shfl_xor_sync(0xffffffffu, v[i], o);
+      v[i] = MAX ? fmaxf(v[i], r) : v[i] + r;
+    }
+  }
+#pragma unroll
+  for (int o = NC / 2; o >= 1; o >>= 1) {
     const bool upper = (lane & o) != 0;
 #pragma unroll
     for (int i = 0; i < o; ++i) {
@@ -118,26 +146,216 @@ __device__ __forceinline__ float warp_columns(float (&v)[32], int lane) {
   return v[0];
 }
 
+template <int NC>
+__device__ __forceinline__ void tmem_ld_cols(uint32_t taddr, uint32_t (&r)[NC]) {
+  if constexpr (NC == 32) tmem_ld32(taddr, r); else tmem_ld16(taddr, r);
+}
+template <int NC>
+__device__ __forceinline__ void tmem_st_cols(uint32_t taddr, const uint32_t (&r)[NC]) {
+  if constexpr (NC == 32) tmem_st32(taddr, r); else tmem_st16(taddr, r);
+}
+
+// Barrier slots in shared memory (kDecOffBar): K ring full/empty, V ring
+// full/empty (kDecStages each), then the named singles below.
+enum DecBar : int {
+  kBarKFull = 0,
+  kBarKEmpty = kDecStages,
+  kBarVFull = 2 * kDecStages,
+  kBarVEmpty = 3 * kDecStages,
+  kBarQFull = 4 * kDecStages,  // 128 arrivals
+  kBarQEmpty,
+  kBarSFull,                   // [2]
+  kBarSFree = kBarSFull + 2,   // [2] 128 arrivals
+  kBarPFull = kBarSFree + 2,   // [2] 128 arrivals
+  kBarPFree = kBarPFull + 2,   // [2]
+  kBarODone = kBarPFree + 2,   // every PV
+  kBarOFinal,                  // last PV of an item
+  kBarOFree,                   // 128 arrivals: O read out
+  kBarRed,                     // 128 arrivals
+  kBarDrain,
+  kBarCount
+};
+
+// The tiles of one item with NC (16 or 32) query columns, then the item's
+// partial. Returns false when a wait gave up.
+template <int NC>
+__device__ __forceinline__ bool dec_softmax_item(const DecParams& p, uint8_t* smem,
+                                                 volatile int* abort_flag,
+                                                 uint32_t tmem_base, int qw, int lane,
+                                                 const DecItem& it, int w, uint32_t& kt,
+                                                 uint32_t& rb, uint32_t ic) {
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kDecOffBar);
+  float* red = reinterpret_cast<float*>(smem + kDecOffRed);
+  const int t = qw * 32 + lane;
+  const uint32_t lane_off = static_cast<uint32_t>(qw * 32) << 16;
+  const uint32_t tmem_o = tmem_base + 64;
+  const int ncol = it.nq * p.group;
+  const int n_tiles = (it.t_end - it.t_begin + 127) / 128;
+  float mref[NC], lsum[NC];
+#pragma unroll
+  for (int i = 0; i < NC; ++i) {
+    mref[i] = -INFINITY;
+    lsum[i] = 0.f;
+  }
+  for (int j = 0; j < n_tiles; ++j) {
+    const uint32_t tt = kt + j;
+    const int b = tt & 1;
+    const int t0 = it.t_begin + j * 128;
+    const bool ready = mbar_wait(&(bars + kBarSFull)[b], (tt >> 1) & 1, abort_flag);
+    if (!__all_sync(0xffffffffu, ready)) return false;
+    tc_fence_after();
+    float s[NC];
+    {
+      uint32_t u[NC];
+      tmem_ld_cols<NC>(tmem_base + lane_off + b * 32, u);
+      tmem_wait_ld();
+#pragma unroll
+      for (int i = 0; i < NC; ++i) s[i] = __uint_as_float(u[i]);
+    }
+    tc_fence_before();
+    mbar_arrive(&(bars + kBarSFree)[b]);
+    // Column n = query row n / group: key visible iff key <= pos0 + n / group,
+    // i.e. n >= (key - pos0) * group.
+    const int key = t0 + t;
+    const int thr = key > it.pos0 ? min((key - it.pos0) * p.group, NC) : 0;
+#pragma unroll
+    for (int n = 0; n < NC; ++n)
+      s[n] = (n >= thr && n < ncol) ? s[n] * p.scale_log2 : -INFINITY;
+    // Keys past the last written one (only in the last tile): zero their
+    // V rows, once V has landed, so 0 * stale data cannot poison P.V.
+    if (t0 + 128 > it.need) {
+      const int st = tt % kDecStages;
+      const bool vin = mbar_wait(&(bars + kBarVFull)[st], (tt / kDecStages) & 1, abort_flag);
+      if (!__all_sync(0xffffffffu, vin)) return false;
+      if (key >= it.need) {
+        uint8_t* vrow = smem + kDecOffV + st * kDecTile + t * 128;
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          *reinterpret_cast<uint4*>(vrow + q * 16) = make_uint4(0, 0, 0, 0);
+          *reinterpret_cast<uint4*>(vrow + kDecHalf + q * 16) = make_uint4(0, 0, 0, 0);
+        }
+      }
+    }
+    // ---- tile max per column: warp reduction, then across the 4 warps
+    float tmp[NC];
+#pragma unroll
+    for (int n = 0; n < NC; ++n) tmp[n] = s[n];
+    float* rbuf = red + (rb & 1) * 128;
+    rbuf[qw * 32 + lane] = warp_columns<NC, true>(tmp, lane);
+    mbar_arrive((bars + kBarRed));
+    const bool synced = mbar_wait((bars + kBarRed), rb & 1, abort_flag);
+    ++rb;
+    if (!__all_sync(0xffffffffu, synced)) return false;
+    const float mcol = fmaxf(fmaxf(rbuf[lane], rbuf[32 + lane]),
+                             fmaxf(rbuf[64 + lane], rbuf[96 + lane]));
+    // lane l owns column l % NC: rescale when any column outgrew its reference
+    float my_ref = -INFINITY;
+#pragma unroll
+    for (int n = 0; n < NC; ++n)
+      if (n == (lane & (NC - 1))) my_ref = mref[n];
+    const bool grow = j == 0 ? (mcol > -INFINITY) : (mcol > my_ref + kDecRescale);
+    if (__any_sync(0xffffffffu, grow)) {
+      const float mnew = fmaxf(my_ref, mcol);
+      const float alpha = (my_ref == -INFINITY) ? 0.f : ex2_approx(my_ref - mnew);
+      if (j > 0) {
+        // PV_{j-1} must have landed (PV_{j-2} has: S_j was issued after it)
+        const bool done = mbar_wait((bars + kBarODone), (tt - 1) & 1, abort_flag);
+        if (!__all_sync(0xffffffffu, done)) return false;
+        tc_fence_after();
+        uint32_t u[NC];
+        tmem_ld_cols<NC>(tmem_o + lane_off, u);
+        tmem_wait_ld();
+#pragma unroll
+        for (int n = 0; n < NC; ++n)
+          u[n] = __float_as_uint(__uint_as_float(u[n]) * __shfl_sync(0xffffffffu, alpha, n));
+        tmem_st_cols<NC>(tmem_o + lane_off, u);
+        tmem_wait_st();
+      }
+#pragma unroll
+      for (int n = 0; n < NC; ++n) {
+        lsum[n] *= __shfl_sync(0xffffffffu, alpha, n);
+        mref[n] = __shfl_sync(0xffffffffu, mnew, n);
+      }
+    }
+    // ---- P^T: row n, key t (two 128-byte-swizzled halves of 64 keys)
+    const bool pfree = mbar_wait(&(bars + kBarPFree)[b], ((tt >> 1) & 1) ^ 1, abort_flag);
+    if (!__all_sync(0xffffffffu, pfree)) return false;
+    uint8_t* pbase = smem + kDecOffP + b * kDecQBytes + (t >> 6) * (kDecQBytes / 2);
+    const int kb = (t & 63) * 2;
+    const int kq = kb >> 4, kr = kb & 15;
+#pragma unroll
+    for (int n = 0; n < NC; ++n) {
+      const float e = s[n] == -INFINITY ? 0.f : ex2_approx(s[n] - mref[n]);
+      lsum[n] += e;
+      *reinterpret_cast<__nv_bfloat16*>(pbase + n * 128 + ((kq ^ (n & 7)) << 4) + kr) =
+          __float2bfloat16_rn(e);
+    }
+    fence_async_smem();
+    tc_fence_before();
+    mbar_arrive(&(bars + kBarPFull)[b]);
+  }
+  kt += n_tiles;
+  // ---- item partial: O^T (unnormalised), m and l per column
+  const bool fin = mbar_wait((bars + kBarOFinal), ic & 1, abort_flag);
+  if (!__all_sync(0xffffffffu, fin)) return false;
+  tc_fence_after();
+  {
+    uint32_t u[NC];
+    tmem_ld_cols<NC>(tmem_o + lane_off, u);
+    tmem_wait_ld();
+    float* o = p.ws_o + static_cast<long long>(w) * 32 * 128 + t;
+#pragma unroll
+    for (int n = 0; n < NC; ++n)
+      if (n < ncol) o[n * 128] = __uint_as_float(u[n]);
+  }
+  tc_fence_before();
+  mbar_arrive((bars + kBarOFree));
+  // l: sum over the 128 threads, column l on lane l
+  float* rbuf = red + (rb & 1) * 128;
+  rbuf[qw * 32 + lane] = warp_columns<NC, false>(lsum, lane);
+  mbar_arrive((bars + kBarRed));
+  const bool synced = mbar_wait((bars + kBarRed), rb & 1, abort_flag);
+  ++rb;
+  if (!__all_sync(0xffffffffu, synced)) return false;
+  if (qw == 0 && lane < NC) {
+    float my_ref = -INFINITY;
+#pragma unroll
+    for (int n = 0; n < NC; ++n)
+      if (n == lane) my_ref = mref[n];
+    p.ws_ml[static_cast<long long>(w) * 64 + lane] = my_ref;
+    p.ws_ml[static_cast<long long>(w) * 64 + 32 + lane] =
+        rbuf[lane] + rbuf[32 + lane] + rbuf[64 + lane] + rbuf[96 + lane];
+  }
+  return true;
+}
+
+// NC = 16 when every item has at most 16 query columns (decode of one or two
+// rows at 8 query heads per kv head), else 32.
+template <int NC>
 __global__ void __launch_bounds__(kDecThreads, 1)
-    decode_attn_kernel(const __grid_constant__ CUtensorMap tmKV, const DecParams p,
+    decode_attn_kernel(const __grid_constant__ CUtensorMap tmKV,
+                       const __grid_constant__ DecParams p,
                        int n_items) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   float* red = reinterpret_cast<float*>(smem + kDecOffRed);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kDecOffBar);
-  uint64_t* kv_full = bars;                   // [3]
-  uint64_t* kv_empty = bars + kDecStages;     // [3]
-  uint64_t* q_full = bars + 2 * kDecStages;   // 128 arrivals
-  uint64_t* q_empty = q_full + 1;
-  uint64_t* s_full = q_full + 2;
-  uint64_t* s_free = q_full + 3;              // 128 arrivals
-  uint64_t* p_full = q_full + 4;              // 128 arrivals
-  uint64_t* p_free = q_full + 5;
-  uint64_t* o_final = q_full + 6;
-  uint64_t* o_free = q_full + 7;              // 128 arrivals
-  uint64_t* red_bar = q_full + 8;             // 128 arrivals
-  uint64_t* drain = q_full + 9;
+  uint64_t* k_full = bars + kBarKFull;
+  uint64_t* k_empty = bars + kBarKEmpty;
+  uint64_t* v_full = bars + kBarVFull;
+  uint64_t* v_empty = bars + kBarVEmpty;
+  uint64_t* q_full = bars + kBarQFull;
+  uint64_t* q_empty = bars + kBarQEmpty;
+  uint64_t* s_full = bars + kBarSFull;
+  uint64_t* s_free = bars + kBarSFree;
+  uint64_t* p_full = bars + kBarPFull;
+  uint64_t* p_free = bars + kBarPFree;
+  uint64_t* o_done = bars + kBarODone;
+  uint64_t* o_final = bars + kBarOFinal;
+  uint64_t* o_free = bars + kBarOFree;
+  uint64_t* red_bar = bars + kBarRed;
+  uint64_t* drain = bars + kBarDrain;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kDecBars);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -147,15 +365,20 @@ __global__ void __launch_bounds__(kDecThreads, 1)
   if (threadIdx.x == 0) {
     *abort_flag = 0;
     for (int i = 0; i < kDecStages; ++i) {
-      mbar_init(&kv_full[i], 1);
-      mbar_init(&kv_empty[i], 1);
+      mbar_init(&k_full[i], 1);
+      mbar_init(&k_empty[i], 1);
+      mbar_init(&v_full[i], 1);
+      mbar_init(&v_empty[i], 1);
     }
     mbar_init(q_full, 128);
     mbar_init(q_empty, 1);
-    mbar_init(s_full, 1);
-    mbar_init(s_free, 128);
-    mbar_init(p_full, 128);
-    mbar_init(p_free, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&s_free[i], 128);
+      mbar_init(&p_full[i], 128);
+      mbar_init(&p_free[i], 1);
+    }
+    mbar_init(o_done, 1);
     mbar_init(o_final, 1);
     mbar_init(o_free, 128);
     mbar_init(red_bar, 128);
@@ -164,121 +387,136 @@ __global__ void __launch_bounds__(kDecThreads, 1)
   }
   if (warp == 0 && lane == 0) tma_prefetch_desc(&tmKV);
   if (warp == 1) {
-    tmem_alloc(tmem_slot, 64);
+    tmem_alloc(tmem_slot, 128);
     tmem_relinquish();
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  const uint32_t tmem_s = *tmem_slot;       // S^T: 32 columns
-  const uint32_t tmem_o = tmem_s + kDecMaxN;  // O^T: 32 columns
+  const uint32_t tmem_base = *tmem_slot;    // S^T buffers: cols [0,32), [32,64)
+  const uint32_t tmem_o = tmem_base + 64;   // O^T: cols [64,96)
 
   if (warp == 0) {
-    if (lane == 0) {
-      // ------------------------------------------------ TMA producer
-      uint32_t kt = 0;
-      bool ok = true;
-      for (int w = blockIdx.x; w < n_items && ok; w += gridDim.x) {
-        const DecItem it = dec_item(p, w);
-        for (int t0 = it.t_begin; t0 < it.t_end; t0 += 128, ++kt) {
-          const int st = kt % kDecStages;
-          if (!mbar_wait(&kv_empty[st], ((kt / kDecStages) & 1) ^ 1, abort_flag)) {
-            ok = false;
-            break;
+    // -------------------------------------------------- TMA producer
+    // The whole warp reads the item's page ids into shared memory (off the
+    // load path), then issues each tile's boxes, K before V.
+    int* page_ids = reinterpret_cast<int*>(smem + kDecOffPages);
+    uint32_t kt = 0;
+    bool ok = true;
+    for (int w = blockIdx.x; w < n_items && ok; w += gridDim.x) {
+      const DecItem it = dec_item(p, w);
+      if (it.t_begin >= it.t_end) continue;
+      const int pg0 = it.t_begin / p.block_size;
+      const int npg = (it.t_end - 1) / p.block_size - pg0 + 1;
+      const int bt0 = p.bt_off[it.s], bt_n = p.bt_off[it.s + 1] - bt0;
+      for (int i = lane; i < npg; i += 32) {
+        const int idx = pg0 + i;
+        const int page = idx < bt_n ? p.bt[bt0 + idx] : -1;
+        // Pages outside the pool or the table are reported and skipped
+        // (their keys then hold stale data: the result is undefined but
+        // every access stays inside the pool).
+        const bool good = page >= 0 && page < p.num_pages;
+        if (!good && p.status) atomicOr(p.status, kDevBadInput);
+        page_ids[i] = good ? page : -1;
+      }
+      __syncwarp();
+      // Lane 0 claims the ring slot and sets the byte count; lane sg then
+      // issues page segment sg's boxes (up to 8 per 128-key tile), so small
+      // pages do not serialise on one issuing thread.
+      for (int t0 = it.t_begin; t0 < it.t_end && ok; t0 += 128, ++kt) {
+        const int st = kt % kDecStages;
+        const uint32_t eph = ((kt / kDecStages) & 1) ^ 1;
+        const int t1 = min(t0 + 128, it.t_end);
+        const int segs = (t1 - t0 + p.box_rows - 1) / p.box_rows;
+        const int my_page =
+            lane < segs ? page_ids[(t0 + lane * p.box_rows) / p.block_size - pg0] : -1;
+        const uint32_t loaded = __popc(__ballot_sync(0xffffffffu, my_page >= 0));
+        const uint32_t bytes = loaded * p.box_rows * 128u * 2u;
+        for (int kv = 0; kv < 2 && ok; ++kv) {
+          uint64_t* full = kv ? &v_full[st] : &k_full[st];
+          bool got = true;
+          if (lane == 0) {
+            got = mbar_wait(kv ? &v_empty[st] : &k_empty[st], eph, abort_flag);
+            if (got) mbar_arrive_expect_tx(full, bytes);
           }
-          const int t1 = min(t0 + 128, it.t_end);
-          const int segs = (t1 - t0 + p.box_rows - 1) / p.box_rows;
-          const int bt0 = p.bt_off[it.s], bt_n = p.bt_off[it.s + 1] - bt0;
-          // Pages outside the pool or the sequence's table are reported and
-          // skipped (their keys then hold stale data: the result is undefined
-          // but every access stays inside the pool).
-          uint32_t loaded = 0;
-          int page_of[8];
-#pragma unroll
-          for (int sg = 0; sg < 8; ++sg) {
-            page_of[sg] = -1;
-            if (sg < segs) {
-              const int idx = (t0 + sg * p.box_rows) / p.block_size;
-              const int page = idx < bt_n ? p.bt[bt0 + idx] : -1;
-              if (page >= 0 && page < p.num_pages) {
-                page_of[sg] = page;
-                ++loaded;
-              } else if (p.status) {
-                atomicOr(p.status, kDevBadInput);
-              }
-            }
-          }
-          mbar_arrive_expect_tx(&kv_full[st], loaded * p.box_rows * 128u * 2u * 2u);
-          uint8_t* kd = smem + st * kDecStageBytes;
-          uint8_t* vd = kd + 2 * kDecHalf;
-#pragma unroll
-          for (int sg = 0; sg < 8; ++sg) {
-            if (page_of[sg] < 0) continue;
-            const int tok = t0 + sg * p.box_rows;
-            const long long row = page_of[sg] * p.page_rows + p.layer * p.layer_rows +
-                                  tok % p.block_size;
-            const int krow = static_cast<int>(row), vrow = static_cast<int>(row + p.kv_rows);
-            const uint32_t off = sg * p.box_rows * 128u;
-            tma_load_2d(kd + off, &tmKV, &kv_full[st], it.kh * 128, krow);
-            tma_load_2d(kd + kDecHalf + off, &tmKV, &kv_full[st], it.kh * 128 + 64, krow);
-            tma_load_2d(vd + off, &tmKV, &kv_full[st], it.kh * 128, vrow);
-            tma_load_2d(vd + kDecHalf + off, &tmKV, &kv_full[st], it.kh * 128 + 64, vrow);
+          ok = __shfl_sync(0xffffffffu, got, 0);
+          if (!ok) break;
+          if (my_page >= 0) {
+            const int tok = t0 + lane * p.box_rows;
+            const int row = static_cast<int>(my_page * p.page_rows + p.layer * p.layer_rows +
+                                             kv * p.kv_rows + tok % p.block_size);
+            uint8_t* dst = smem + (kv ? kDecOffV : kDecOffK) + st * kDecTile +
+                           lane * p.box_rows * 128u;
+            tma_load_2d(dst, &tmKV, full, it.kh * 128, row);
+            tma_load_2d(dst + kDecHalf, &tmKV, full, it.kh * 128 + 64, row);
           }
         }
       }
+      __syncwarp();
     }
   } else if (warp == 1) {
     if (lane == 0) {
       // ------------------------------------------------ MMA issuer
+      // Order per item: S_0, then for each tile j: S_{j+1}, PV_j, so the
+      // softmax of tile j overlaps the next tile's S.
       const uint32_t q_addr = smem_u32(smem + kDecOffQ);
-      const uint32_t p_addr = smem_u32(smem + kDecOffP);
       uint32_t kt = 0, ic = 0;
       bool ok = true;
       for (int w = blockIdx.x; w < n_items && ok; w += gridDim.x) {
         const DecItem it = dec_item(p, w);
         if (it.t_begin >= it.t_end) continue;
+        const int n = (it.t_end - it.t_begin + 127) / 128;
         const int npad = (it.nq * p.group + 15) & ~15;
         const uint32_t idesc_s = idesc_bf16(128, npad, 0, 0);
         const uint32_t idesc_o = idesc_bf16(128, npad, 1, 0);
         if (!mbar_wait(q_full, ic & 1, abort_flag)) { ok = false; break; }
-        bool first = true;
-        for (int t0 = it.t_begin; t0 < it.t_end; t0 += 128, ++kt) {
-          const int st = kt % kDecStages;
-          if (!mbar_wait(&kv_full[st], (kt / kDecStages) & 1, abort_flag) ||
-              !mbar_wait(s_free, (kt & 1) ^ 1, abort_flag)) {
-            ok = false;
-            break;
-          }
+        auto issue_s = [&](int j) -> bool {
+          const uint32_t t = kt + j;
+          const int st = t % kDecStages, b = t & 1;
+          if (!mbar_wait(&k_full[st], (t / kDecStages) & 1, abort_flag) ||
+              !mbar_wait(&s_free[b], ((t >> 1) & 1) ^ 1, abort_flag))
+            return false;
           tc_fence_after();
-          const uint32_t k_addr = smem_u32(smem + st * kDecStageBytes);
-          const uint32_t v_addr = k_addr + 2 * kDecHalf;
+          const uint32_t k_addr = smem_u32(smem + kDecOffK + st * kDecTile);
 #pragma unroll
           for (int kk = 0; kk < 8; ++kk)
-            mma_f16_ss(tmem_s,
+            mma_f16_ss(tmem_base + b * 32,
                        sdesc_sw128(k_addr + (kk >> 2) * kDecHalf + (kk & 3) * 32, 0, 1024),
                        sdesc_sw128(q_addr + (kk >> 2) * (kDecQBytes / 2) + (kk & 3) * 32, 0,
                                    1024),
                        idesc_s, kk > 0);
-          mma_commit(s_full);
-          if (t0 + 128 >= it.t_end) mma_commit(q_empty);
-          if (!mbar_wait(p_full, kt & 1, abort_flag) ||
-              (first && !mbar_wait(o_free, (ic & 1) ^ 1, abort_flag))) {
+          mma_commit(&s_full[b]);
+          mma_commit(&k_empty[st]);
+          if (j == n - 1) mma_commit(q_empty);
+          return true;
+        };
+        if (!issue_s(0)) { ok = false; break; }
+        for (int j = 0; j < n; ++j) {
+          if (j + 1 < n && !issue_s(j + 1)) { ok = false; break; }
+          const uint32_t t = kt + j;
+          const int st = t % kDecStages, b = t & 1;
+          if (!mbar_wait(&v_full[st], (t / kDecStages) & 1, abort_flag) ||
+              !mbar_wait(&p_full[b], (t >> 1) & 1, abort_flag) ||
+              (j == 0 && !mbar_wait(o_free, (ic & 1) ^ 1, abort_flag))) {
             ok = false;
             break;
           }
           tc_fence_after();
+          const uint32_t v_addr = smem_u32(smem + kDecOffV + st * kDecTile);
+          const uint32_t p_addr = smem_u32(smem + kDecOffP + b * kDecQBytes);
 #pragma unroll
           for (int kk = 0; kk < 8; ++kk)
             mma_f16_ss(tmem_o, sdesc_sw128(v_addr + kk * 2048, kDecHalf, 1024),
                        sdesc_sw128(p_addr + (kk >> 2) * (kDecQBytes / 2) + (kk & 3) * 32, 0,
                                    1024),
-                       idesc_o, (!first || kk > 0) ? 1u : 0u);
-          first = false;
-          mma_commit(&kv_empty[st]);
-          mma_commit(p_free);
+                       idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
+          mma_commit(&v_empty[st]);
+          mma_commit(&p_free[b]);
+          mma_commit(o_done);
         }
         if (!ok) break;
         mma_commit(o_final);
+        kt += n;
         ++ic;
       }
       mma_commit(drain);
@@ -291,7 +529,6 @@ __global__ void __launch_bounds__(kDecThreads, 1)
     const int t = qw * 32 + lane;               // key within the tile; head dim
     const uint32_t lane_off = static_cast<uint32_t>(qw * 32) << 16;
     uint8_t* qs = smem + kDecOffQ;
-    uint8_t* ps = smem + kDecOffP;
     uint32_t kt = 0, ic = 0, rb = 0;
     bool ok = true;
     for (int w = blockIdx.x; w < n_items && ok; w += gridDim.x) {
@@ -328,132 +565,9 @@ __global__ void __launch_bounds__(kDecThreads, 1)
         fence_async_smem();
         mbar_arrive(q_full);
       }
-      float mref[32], lsum[32];
-#pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        mref[i] = -INFINITY;
-        lsum[i] = 0.f;
-      }
-      bool first = true;
-      for (int t0 = it.t_begin; t0 < it.t_end; t0 += 128, ++kt) {
-        const bool ready = mbar_wait(s_full, kt & 1, abort_flag);
-        if (!__all_sync(0xffffffffu, ready)) { ok = false; break; }
-        tc_fence_after();
-        float s[32];
-        {
-          uint32_t u[32];
-          tmem_ld32(tmem_s + lane_off, u);
-          tmem_wait_ld();
-#pragma unroll
-          for (int i = 0; i < 32; ++i) s[i] = __uint_as_float(u[i]);
-        }
-        tc_fence_before();
-        mbar_arrive(s_free);
-        const int key = t0 + t;
-#pragma unroll
-        for (int n = 0; n < 32; ++n) {
-          const bool valid = n < ncol && key <= it.pos0 + n / p.group;
-          s[n] = valid ? s[n] * p.scale_log2 : -INFINITY;
-        }
-        // Keys past the last written one: zero their V rows so 0 * stale
-        // data cannot poison the P.V product.
-        if (key >= it.need) {
-          uint8_t* vrow = smem + (kt % kDecStages) * kDecStageBytes + 2 * kDecHalf + t * 128;
-#pragma unroll
-          for (int c = 0; c < 8; ++c) {
-            *reinterpret_cast<uint4*>(vrow + c * 16) = make_uint4(0, 0, 0, 0);
-            *reinterpret_cast<uint4*>(vrow + kDecHalf + c * 16) = make_uint4(0, 0, 0, 0);
-          }
-        }
-        // ---- tile max per column: warp transpose reduction, then 4 warps
-        float tmp[32];
-#pragma unroll
-        for (int n = 0; n < 32; ++n) tmp[n] = s[n];
-        float* rbuf = red + (rb & 1) * 128;
-        rbuf[qw * 32 + lane] = warp_columns<true>(tmp, lane);
-        mbar_arrive(red_bar);
-        const bool synced = mbar_wait(red_bar, rb & 1, abort_flag);
-        ++rb;
-        if (!__all_sync(0xffffffffu, synced)) { ok = false; break; }
-        const float mcol = fmaxf(fmaxf(rbuf[lane], rbuf[32 + lane]),
-                                 fmaxf(rbuf[64 + lane], rbuf[96 + lane]));
-        // lane l owns column l: rescale when any column outgrew its reference
-        float my_ref = -INFINITY;
-#pragma unroll
-        for (int n = 0; n < 32; ++n)
-          if (n == lane) my_ref = mref[n];
-        const bool grow = first ? (mcol > -INFINITY) : (mcol > my_ref + kDecRescale);
-        if (__any_sync(0xffffffffu, grow)) {
-          const float mnew = fmaxf(my_ref, mcol);
-          const float alpha = (my_ref == -INFINITY) ? 0.f : ex2_approx(my_ref - mnew);
-          if (!first) {
-            // O^T row t (head dim t): scale column n by column n's alpha
-            uint32_t u[32];
-            tmem_ld32(tmem_o + lane_off, u);
-            tmem_wait_ld();
-#pragma unroll
-            for (int n = 0; n < 32; ++n)
-              u[n] = __float_as_uint(__uint_as_float(u[n]) *
-                                     __shfl_sync(0xffffffffu, alpha, n));
-            tmem_st32(tmem_o + lane_off, u);
-            tmem_wait_st();
-          }
-#pragma unroll
-          for (int n = 0; n < 32; ++n) {
-            const float a = __shfl_sync(0xffffffffu, alpha, n);
-            lsum[n] *= a;
-            mref[n] = __shfl_sync(0xffffffffu, mnew, n);
-          }
-        }
-        first = false;
-        // ---- P^T: row n, key t (two 128-byte-swizzled halves of 64 keys)
-        const bool pfree = mbar_wait(p_free, (kt & 1) ^ 1, abort_flag);
-        if (!__all_sync(0xffffffffu, pfree)) { ok = false; break; }
-        uint8_t* pbase = ps + (t >> 6) * (kDecQBytes / 2);
-        const int kb = (t & 63) * 2;
-#pragma unroll
-        for (int n = 0; n < 32; ++n) {
-          const float e = s[n] == -INFINITY ? 0.f : ex2_approx(s[n] - mref[n]);
-          lsum[n] += e;
-          *reinterpret_cast<__nv_bfloat16*>(pbase + n * 128 + (((kb >> 4) ^ (n & 7)) << 4) +
-                                            (kb & 15)) = __float2bfloat16_rn(e);
-        }
-        fence_async_smem();
-        tc_fence_before();
-        mbar_arrive(p_full);
-      }
-      if (!ok) break;
-      // ---- item partial: O^T (unnormalised), m and l per column
-      const bool fin = mbar_wait(o_final, ic & 1, abort_flag);
-      if (!__all_sync(0xffffffffu, fin)) { ok = false; break; }
-      tc_fence_after();
-      {
-        uint32_t u[32];
-        tmem_ld32(tmem_o + lane_off, u);
-        tmem_wait_ld();
-        float* o = p.ws_o + static_cast<long long>(w) * 32 * 128 + t;
-#pragma unroll
-        for (int n = 0; n < 32; ++n)
-          if (n < ncol) o[n * 128] = __uint_as_float(u[n]);
-      }
-      tc_fence_before();
-      mbar_arrive(o_free);
-      // l: sum over the 128 threads, column l on lane l
-      float* rbuf = red + (rb & 1) * 128;
-      rbuf[qw * 32 + lane] = warp_columns<false>(lsum, lane);
-      mbar_arrive(red_bar);
-      const bool synced = mbar_wait(red_bar, rb & 1, abort_flag);
-      ++rb;
-      if (!__all_sync(0xffffffffu, synced)) { ok = false; break; }
-      if (qw == 0) {
-        float my_ref = -INFINITY;
-#pragma unroll
-        for (int n = 0; n < 32; ++n)
-          if (n == lane) my_ref = mref[n];
-        p.ws_ml[static_cast<long long>(w) * 64 + lane] = my_ref;
-        p.ws_ml[static_cast<long long>(w) * 64 + 32 + lane] =
-            rbuf[lane] + rbuf[32 + lane] + rbuf[64 + lane] + rbuf[96 + lane];
-      }
+      const bool done =
+          dec_softmax_item<NC>(p, smem, abort_flag, tmem_base, qw, lane, it, w, kt, rb, ic);
+      if (!done) { ok = false; break; }
       ++ic;
     }
   }
@@ -467,7 +581,7 @@ __global__ void __launch_bounds__(kDecThreads, 1)
   if (warp == 1) {
     __syncwarp();
     tc_fence_after();
-    tmem_dealloc(tmem_s, 64);
+    tmem_dealloc(tmem_base, 128);
   }
 }
 
@@ -486,7 +600,7 @@ __global__ void __launch_bounds__(128)
   const int nq = min(p.nqg, q1 - r_begin);
   if (nq <= 0 || n >= nq * p.group) return;
   const int need = p.q_pos[s] + (r_begin - q0) + nq;
-  const int chunks = (need + kDecChunk - 1) / kDecChunk;
+  const int chunks = dec_chunks(need);
   const long long w0 = static_cast<long long>(base) * p.C;
   float M = -INFINITY;
   for (int c = 0; c < chunks; ++c) M = fmaxf(M, p.ws_ml[(w0 + c) * 64 + n]);
@@ -705,9 +819,11 @@ extern "C" int kvm_sm100_attention_decode_paged(
                          CU_TENSOR_MAP_SWIZZLE_128B));
   const int grid = items < dev->sm_count ? int(items) : dev->sm_count;
   constexpr size_t smem = dec_smem_bytes();
-  KVM_CUDA_TRY(cudaFuncSetAttribute(decode_attn_kernel,
-                                    cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
-  decode_attn_kernel<<<grid, kDecThreads, smem, st>>>(tkv, p, int(items));
+  auto kern = min(max_q_rows, p.nqg) * group <= 16 ? decode_attn_kernel<16>
+                                                   : decode_attn_kernel<32>;
+  KVM_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    int(smem)));
+  kern<<<grid, kDecThreads, smem, st>>>(tkv, p, int(items));
   KVM_CUDA_TRY(cudaGetLastError());
   dim3 cgrid(static_cast<unsigned>(S * HKV * p.QG), kDecMaxN);
   decode_combine_kernel<<<cgrid, 128, 0, st>>>(p, static_cast<__nv_bfloat16*>(out), ldo);
