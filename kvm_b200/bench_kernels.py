@@ -10,6 +10,8 @@ bench.py's format.
         352 MB of weights per step (> L2).
   fp8   W8A8 block-scaled GEMM [M,8192] x [8192,28672] e4m3 with 128x128 fp32
         scales, bf16 out, M in {16, 128, 1024}; 235 MB of weights (> L2).
+  attn  the decoder layer's causal GQA attention alone: q [4*2048, 64*128],
+        k/v [4*2048, 8*128] bf16 (168 MB > L2), one fused launch.
   decode  one decode step of 64 sequences over a paged KV cache: 4096 cached
         tokens each, 64 query / 8 kv heads of 128 (the decoder layer's heads),
         16-token pages scattered over the pool (page_first); a step writes
@@ -159,9 +161,35 @@ def run_tp(args, peaks, ClockSampler) -> int:
     return 0
 
 
+def run_attn(args, peaks, ClockSampler, dev, g) -> int:
+    B, L, HQ, HKV = 4, 2048, 64, 8
+    q = torch.randn((B * L, HQ * 128), generator=g, device=dev).to(torch.bfloat16)
+    k = torch.randn((B * L, HKV * 128), generator=g, device=dev).to(torch.bfloat16)
+    v = torch.randn((B * L, HKV * 128), generator=g, device=dev).to(torch.bfloat16)
+    out = torch.empty_like(q)
+    steps, warmup = args.steps, max(args.warmup, 3)
+    fn = lambda: ops.attention_prefill(q, k, v, batch=B, heads_q=HQ, heads_kv=HKV, out=out)
+    with ClockSampler(0) as ck:
+        t0 = time.time()
+        ms = _time(fn, steps, warmup)
+        t1 = time.time()
+    # causal: keys 0..pos for each query -> 2 * (L (L + 1) / 2) * 128 * 2 per head
+    flop = 4.0 * B * HQ * 128 * (L * (L + 1) / 2)
+    tf = flop / (ms / 1e3) / 1e12
+    _line(args, ck, t0, t1, metric="causal attention TFLOP/s", value=tf, unit="TFLOP/s",
+          ms_per_step=ms, dtype="bf16",
+          config={"workload": f"causal_gqa_attention_B{B}_L{L}_HQ{HQ}_HKV{HKV}_hd128",
+                  "l2": "168 MB of q/k/v > L2"},
+          roofline={"bound": "tensor", "achieved": tf, "peak": peaks["bf16"],
+                    "unit": "TFLOP/s", "frac": tf / peaks["bf16"], "traffic": None,
+                    "kernel": "attn_fwd_kernel"},
+          gpu_launches=steps)
+    return 0
+
+
 def run_decode(args, peaks, ClockSampler, dev, g) -> int:
     from .kvcache import PagedKVCache
-    S, ctx, HQ, HKV, bs = 64, 4096, 64, 8, 16
+    S, ctx, HQ, HKV, bs = args.seqs, 4096, 64, 8, 16
     keys = ctx + 1
     per_seq = (keys + bs - 1) // bs
     pages = S * per_seq
@@ -195,9 +223,9 @@ def run_decode(args, peaks, ClockSampler, dev, g) -> int:
     flop = 4.0 * S * HQ * keys * 128
     _line(args, ck, t0, t1, metric="paged decode attention GB/s", value=gbs, unit="GB/s",
           ms_per_step=ms, dtype="bf16",
-          config={"workload": "paged_decode_S64_ctx4096_HQ64_HKV8_hd128_bs16",
+          config={"workload": f"paged_decode_S{S}_ctx4096_HQ64_HKV8_hd128_bs16",
                   "kv_bytes_per_step": kv_bytes, "tflops": flop / (ms / 1e3) / 1e12,
-                  "l2": "1.07 GB of K/V per step > L2"},
+                  "l2": f"{kv_bytes / 1e9:.2f} GB of K/V per step > L2"},
           roofline={"bound": "hbm", "achieved": gbs, "peak": peaks["hbm"], "unit": "GB/s",
                     "frac": gbs / peaks["hbm"], "traffic": None,
                     "kernel": "decode_attn_kernel + combine + kvcache.write"},
@@ -234,6 +262,8 @@ def run(args, peaks, ClockSampler) -> int:
         return 0
     if args.workload == "decode":
         return run_decode(args, peaks, ClockSampler, dev, g)
+    if args.workload == "attn":
+        return run_attn(args, peaks, ClockSampler, dev, g)
     if args.workload == "mlp":
         T, H, F = 4096, 4096, 14336
         x = torch.randn((T, H), generator=g, device=dev).to(torch.bfloat16)
