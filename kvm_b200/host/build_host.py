@@ -48,7 +48,7 @@ FRONTEND = [
     "src/ir/dialect/tile/dialect.cpp",
     "src/transform/kernel_to_task/kernel_to_task.cpp",
 ]
-OURS = ["sm100_device.cpp", "executor.cpp", "kvm_run.cpp"]
+OURS = ["sm100_device.cpp", "executor.cpp", "task_to_tile.cpp", "kvm_run.cpp"]
 REF_TESTS = ["value", "graph", "attr", "serialize", "parse", "kernel_dialect",
              "task_dialect", "tile_dialect", "decomp"]
 
@@ -133,8 +133,8 @@ def build(ref_arg: str | None = None, verbose: bool = False) -> bool:
              *rpaths, *[f"-Wl,-rpath,{d}" for d in libdirs]]
     if not lib.exists():
         raise RuntimeError("build libkvm_sm100.so first (python -m kvm_b200.build)")
-    link(OUT / "kvm_run", [OUT / "kvm_kvm_run.o", OUT / "kvm_executor.o", device, *front],
-         extra)
+    link(OUT / "kvm_run", [OUT / "kvm_kvm_run.o", OUT / "kvm_executor.o",
+                           OUT / "kvm_task_to_tile.o", device, *front], extra)
     if verbose:
         print(f"built host binaries in {OUT}")
     return True

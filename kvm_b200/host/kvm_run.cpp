@@ -2,6 +2,8 @@
 //
 //   kvm_run GRAPH.kvm [--inputs DIR] [--out DIR] [--seed S] [--warmup W]
 //                     [--iters N] [--dump-task] [--lower-only]
+//                     [--tile [--dump-tile]]
+//   kvm_run --verify-tile TILE_GRAPH.kvm
 //
 // The graph is parsed by the reference parser (serial::Parse), lowered by the
 // reference transform with the sm_100a Device target, and executed by the
@@ -10,6 +12,9 @@
 // {std = s} (and {mean = m}) for seeded normal values -- else N(0, 1) from
 // seed S + argument index. Outputs are written to DIR/<name>.bin; a JSON
 // summary (launch plan, time per run, output checksums) goes to stdout.
+// --tile lowers the task graph further to the tile dialect (task_to_tile.h)
+// and checks every tile op against the sm_100a rules (no GPU needed);
+// --verify-tile checks a tile-dialect graph given as text.
 #include <cuda_runtime.h>
 
 #include <any>
@@ -24,8 +29,11 @@
 
 #include "dialect/kernel/dialect.h"
 #include "dialect/task/dialect.h"
+#include "dialect/tile/dialect.h"
+#include "dialect/tile/ops.h"
 #include "executor.h"
 #include "kvm_sm100.h"
+#include "task_to_tile.h"
 #include "serialization/parser.h"
 #include "serialization/registry.h"
 #include "serialization/serializer.h"
@@ -94,7 +102,8 @@ int main(int argc, char** argv) {
   std::string graph_path, in_dir, out_dir;
   uint64_t seed = 0;
   int warmup = 1, iters = 1;
-  bool dump_task = false, lower_only = false;
+  bool dump_task = false, lower_only = false, tile = false, dump_tile = false;
+  std::string verify_tile;
   for (int i = 1; i < argc; ++i) {
     std::string a = argv[i];
     auto next = [&]() -> std::string {
@@ -108,8 +117,32 @@ int main(int argc, char** argv) {
     else if (a == "--iters") iters = std::stoi(next());
     else if (a == "--dump-task") dump_task = true;
     else if (a == "--lower-only") lower_only = true;
+    else if (a == "--tile") tile = true;
+    else if (a == "--dump-tile") dump_tile = true;
+    else if (a == "--verify-tile") verify_tile = next();
     else if (graph_path.empty()) graph_path = a;
     else throw std::runtime_error("unexpected argument " + a);
+  }
+  if (!verify_tile.empty()) {
+    try {
+      kvm::ir::serial::Registry reg;
+      kvm::ir::tile::RegisterTileDialect(reg);
+      kvm::ir::Graph g;
+      kvm::ir::serial::Parse(ReadFile(verify_tile), reg, g);
+      int ops = 0, bad = 0;
+      std::string first;
+      for (const kvm::ir::OpNode* op : g.root()->operations()) {
+        ++ops;
+        kvm::ir::VerifyResult r = kvm::sm100::VerifyTileOp(op);
+        if (!r.ok && bad++ == 0) first = r.error;
+      }
+      std::cout << "{\"tile_ops\": " << ops << ", \"illegal\": " << bad
+                << ", \"first_error\": \"" << first << "\"}" << std::endl;
+      return bad ? 3 : 0;
+    } catch (const std::exception& e) {
+      std::cerr << "kvm_run: " << e.what() << std::endl;
+      return 1;
+    }
   }
   if (graph_path.empty()) {
     std::cerr << "usage: kvm_run GRAPH.kvm [--inputs DIR] [--out DIR] [--seed S]"
@@ -126,6 +159,41 @@ int main(int argc, char** argv) {
       kvm::ir::serial::Registry treg;
       kvm::ir::task::RegisterTaskDialect(treg);
       std::cerr << kvm::ir::serial::Serialize(ex.task_graph(), treg);
+    }
+    if (tile) {  // task graph -> tile graph + sm_100a checks: no GPU needed
+      kvm::ir::Graph tg;
+      kvm::sm100::TileStats st = kvm::sm100::TransformTaskToTile(ex.task_graph(), tg);
+      int ops = 0, bad = 0, dynamic = 0;
+      std::string first;
+      for (const kvm::ir::OpNode* op : tg.root()->operations()) {
+        ++ops;
+        // Products over routed rows (3-D expert weights) keep their task
+        // shape: their tiles depend on the routing and are chosen on the GPU.
+        if (op->op().op.name.rfind("tc.", 0) == 0 &&
+            !op->op().impl.as<kvm::ir::tile::MmaOp>() &&
+            !op->op().impl.as<kvm::ir::tile::MmaAccOp>()) {
+          ++dynamic;
+          continue;
+        }
+        kvm::ir::VerifyResult r = kvm::sm100::VerifyTileOp(op);
+        if (!r.ok && bad++ == 0) first = r.error;
+      }
+      if (dump_tile) {
+        kvm::ir::serial::Registry treg;
+        kvm::ir::tile::RegisterTileDialect(treg);
+        std::cerr << kvm::ir::serial::Serialize(tg, treg);
+      }
+      std::cout << "{\"graph\": \"" << graph_path << "\", \"tile_ops\": " << ops
+                << ", \"mma\": " << st.mma << ", \"loads\": " << st.loads
+                << ", \"stores\": " << st.stores << ", \"copied\": " << st.copied
+                << ", \"dynamic_mma\": " << dynamic
+                << ", \"arguments\": " << tg.root()->arguments().size()
+                << ", \"illegal\": " << bad << ", \"first_error\": \"" << first
+                << "\", \"tiled\": [";
+      for (std::size_t i = 0; i < st.tiled.size(); ++i)
+        std::cout << (i ? ", " : "") << "\"" << st.tiled[i] << "\"";
+      std::cout << "]}" << std::endl;
+      return bad ? 3 : 0;
     }
     if (lower_only) {  // parse + lower + fusion analysis only: no GPU needed
       ex.Plan();
