@@ -304,6 +304,46 @@ int kvm_sm100_attention_prefill_bf16(const void* q, int64_t ldq, const void* k,
                                      void* workspace, int64_t workspace_bytes,
                                      kvm_stream_t stream);
 
+/* ------------------------------------------------------- collectives --- */
+
+/* The kernel dialect's collectives (src/ir/dialect/kernel/dialect.cpp:58-64,
+ * rank sets on kernel/ops.h:39-88) over NCCL on NVLink/NVSwitch, one process
+ * per GPU. A communicator covers `nranks` processes; kvm_sm100_comm_split
+ * derives one for a rank set (a kernel op's `ranks`). Buffers are device
+ * memory of dtype KVM_EW_BF16 / F16 / F32 / I32; `count` is in elements.
+ * Setup is bounded: a rank that does not join within 60 s makes init return
+ * KVM_ERR_TIMEOUT. The reference has no runtime for these ops (they lower to
+ * task.comm.* and stop there, src/device/device.cpp:111-121). */
+typedef struct kvm_comm kvm_comm;
+#define KVM_COMM_ID_BYTES 128
+enum kvm_red_op { KVM_RED_SUM = 0, KVM_RED_MAX = 1 };
+
+int kvm_sm100_comm_unique_id(void* id); /* KVM_COMM_ID_BYTES, made by one rank */
+int kvm_sm100_comm_init(int nranks, int rank, const void* id, kvm_comm** comm);
+/* Every rank of `parent` calls it; members of ranks[0..n) get a
+ * communicator numbered by their position in `ranks`, others get NULL. */
+int kvm_sm100_comm_split(kvm_comm* parent, const int32_t* ranks, int n, kvm_comm** comm);
+int kvm_sm100_comm_rank(const kvm_comm* comm, int* rank, int* nranks);
+int kvm_sm100_comm_destroy(kvm_comm* comm);
+/* comm.all_reduce.sum / .max: recv = op over ranks of send ([count]). */
+int kvm_sm100_all_reduce(kvm_comm* comm, const void* send, void* recv, int64_t count,
+                         int dtype, int op, kvm_stream_t stream);
+/* comm.all_gather: recv [nranks * count] = the ranks' send [count], in rank order. */
+int kvm_sm100_all_gather(kvm_comm* comm, const void* send, void* recv, int64_t count,
+                         int dtype, kvm_stream_t stream);
+/* comm.broadcast: recv = root's send on every rank (send ignored off the root). */
+int kvm_sm100_broadcast(kvm_comm* comm, const void* send, void* recv, int64_t count,
+                        int dtype, int root, kvm_stream_t stream);
+/* comm.send / comm.recv: point to point, matched by peer and order. */
+int kvm_sm100_send(kvm_comm* comm, const void* buf, int64_t count, int dtype, int peer,
+                   kvm_stream_t stream);
+int kvm_sm100_recv(kvm_comm* comm, void* buf, int64_t count, int dtype, int peer,
+                   kvm_stream_t stream);
+/* comm.all_to_all: send [nranks * count] split in rank order; recv [nranks *
+ * count] holds, at chunk p, what rank p sent to this rank. */
+int kvm_sm100_all_to_all(kvm_comm* comm, const void* send, void* recv, int64_t count,
+                         int dtype, kvm_stream_t stream);
+
 /* ------------------------------------------------- paged KV cache --- */
 
 /* A paged K/V pool as KVMeta describes it (src/ir/graph_config.h:20-39):

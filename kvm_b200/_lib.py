@@ -89,6 +89,17 @@ SIGNATURES = {
     "kvm_sm100_fill_normal": (_I, [_P, _I, _I64, C.c_uint64, _F, _F, _P]),
     "kvm_sm100_rmsnorm_bf16": (_I, [_P, _P, _P, _I, _I, _F, _P]),
     "kvm_sm100_silu_mul_bf16": (_I, [_P, _P, _P, _I64, _P]),
+    "kvm_sm100_comm_unique_id": (_I, [_P]),
+    "kvm_sm100_comm_init": (_I, [_I, _I, _P, C.POINTER(C.c_void_p)]),
+    "kvm_sm100_comm_split": (_I, [_P, _P, _I, C.POINTER(C.c_void_p)]),
+    "kvm_sm100_comm_rank": (_I, [_P, C.POINTER(C.c_int), C.POINTER(C.c_int)]),
+    "kvm_sm100_comm_destroy": (_I, [_P]),
+    "kvm_sm100_all_reduce": (_I, [_P, _P, _P, _I64, _I, _I, _P]),
+    "kvm_sm100_all_gather": (_I, [_P, _P, _P, _I64, _I, _P]),
+    "kvm_sm100_broadcast": (_I, [_P, _P, _P, _I64, _I, _I, _P]),
+    "kvm_sm100_send": (_I, [_P, _P, _I64, _I, _I, _P]),
+    "kvm_sm100_recv": (_I, [_P, _P, _I64, _I, _I, _P]),
+    "kvm_sm100_all_to_all": (_I, [_P, _P, _P, _I64, _I, _P]),
     "kvm_sm100_kvcache_write": (_I, [_P, _P, _P, _I64, _P, _I64, _P, _P, _P, _P, _I, _I, _P]),
     "kvm_sm100_kvcache_read": (_I, [_P, _P, _P, _P, _P, _P, _P, _I, _I, _P]),
     "kvm_sm100_attention_decode_workspace": (_I64, [_I, _I, _I, _I, _I]),

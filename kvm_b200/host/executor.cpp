@@ -1,6 +1,7 @@
 // Executor implementation: task graph -> launch plan over the sm_100a C ABI.
 #include "executor.h"
 
+#include <algorithm>
 #include <any>
 #include <cmath>
 #include <cstdlib>
@@ -148,7 +149,37 @@ Executor::Executor(const ir::Graph& kernel, const ir::AttrMap& attrs)
 }
 
 Executor::~Executor() {
+  for (auto& kv : subcomms_)
+    if (kv.second && kv.second != world_) kvm_sm100_comm_destroy(kv.second);
   for (void* p : allocations_) cudaFree(p);
+}
+
+void Executor::SetComm(kvm_comm* world) {
+  if (prepared_) Fail("SetComm must come before Prepare");
+  world_ = world;
+  if (world_ && kvm_sm100_comm_rank(world_, &rank_, &nranks_) != KVM_OK)
+    Fail(std::string("comm: ") + kvm_sm100_last_error());
+}
+
+// The communicator of a rank set, numbered by position in `ranks` (split
+// from the world communicator once; every rank makes the same splits in the
+// same order, since every rank plans the same graph). Null when this rank is
+// not a member.
+kvm_comm* Executor::CommFor(const std::vector<int>& ranks, int* my_index) {
+  *my_index = -1;
+  for (std::size_t i = 0; i < ranks.size(); ++i)
+    if (ranks[i] == rank_) *my_index = int(i);
+  std::vector<int> all(nranks_);
+  for (int i = 0; i < nranks_; ++i) all[i] = i;
+  if (ranks == all) return world_;
+  auto it = subcomms_.find(ranks);
+  if (it != subcomms_.end()) return it->second;
+  std::vector<int32_t> r(ranks.begin(), ranks.end());
+  kvm_comm* sub = nullptr;
+  if (kvm_sm100_comm_split(world_, r.data(), int(r.size()), &sub) != KVM_OK)
+    Fail(std::string("comm split: ") + kvm_sm100_last_error());
+  subcomms_[ranks] = sub;
+  return sub;
 }
 
 void* Executor::Alloc(int64_t bytes) {
@@ -820,16 +851,106 @@ void Executor::PlanComm(const ir::OpNode* op) {
     step_names_.push_back("moe_combine");
     return;
   }
-  // Collectives over a single rank are identities.
+  // The collectives proper (kernel/dialect.cpp:58-64). A rank outside an
+  // op's rank set, and every op over a single rank, passes its input
+  // through; the members exchange over NCCL (kvm_sm100_all_reduce, ...).
   std::vector<int> ranks;
+  int root_rank = -1, peer_from = -1, peer_to = -1;
   if (const auto* r = op->op().impl.as<ir::kernel::AllReduceSum>()) ranks = r->ranks;
   if (const auto* r = op->op().impl.as<ir::kernel::AllReduceMax>()) ranks = r->ranks;
   if (const auto* r = op->op().impl.as<ir::kernel::AllGather>()) ranks = r->ranks;
   if (const auto* r = op->op().impl.as<ir::kernel::AllToAllOp>()) ranks = r->ranks;
-  if (ranks.size() > 1)
-    Fail("'" + name + "' over " + std::to_string(ranks.size()) +
-         " ranks runs through the multi-process runtime, not this single-GPU executor");
-  PlanStore(op->operands()[0], res);
+  if (const auto* r = op->op().impl.as<ir::kernel::BroadcastOp>()) {
+    root_rank = r->from;
+    ranks = r->to;
+    ranks.push_back(r->from);
+    std::sort(ranks.begin(), ranks.end());
+    ranks.erase(std::unique(ranks.begin(), ranks.end()), ranks.end());
+  }
+  if (const auto* r = op->op().impl.as<ir::kernel::SendOp>()) {
+    peer_from = r->from;
+    peer_to = r->to;
+  }
+  if (const auto* r = op->op().impl.as<ir::kernel::RecvOp>()) {
+    peer_from = r->from;
+    peer_to = r->to;
+  }
+  const Buffer in = GlobalOf(op->operands()[0]);
+  const bool p2p = name == "comm.send" || name == "comm.recv";
+  const bool single = p2p ? peer_from == peer_to : ranks.size() <= 1;
+  if (single) {
+    PlanStore(op->operands()[0], res);
+    return;
+  }
+  if (!world_)
+    Fail("'" + name + "' across ranks needs a communicator (kvm_run --rank/--world)");
+  const int dt = EwDtype(in.dtype);
+  const int64_t count = in.numel();
+  const void* src = in.ptr;
+  if (p2p) {
+    if (peer_from < 0 || peer_to < 0 || peer_from >= nranks_ || peer_to >= nranks_)
+      Fail("'" + name + "': rank outside the world");
+    kvm_comm* w = world_;
+    if (name == "comm.send" && rank_ == peer_from) {
+      PlanStore(op->operands()[0], res);  // the sender keeps its value
+      steps_.push_back([=](cudaStream_t st) {
+        return kvm_sm100_send(w, src, count, dt, peer_to, st);
+      });
+      step_names_.push_back("comm_send");
+    } else if (name == "comm.recv" && rank_ == peer_to) {
+      Buffer& out = Materialize(res);
+      if (out.numel() != count) Fail("comm.recv: result shape != operand shape");
+      void* dst = out.ptr;
+      steps_.push_back([=](cudaStream_t st) {
+        return kvm_sm100_recv(w, dst, count, dt, peer_from, st);
+      });
+      step_names_.push_back("comm_recv");
+    } else {
+      PlanStore(op->operands()[0], res);
+    }
+    return;
+  }
+  for (int r : ranks)
+    if (r < 0 || r >= nranks_) Fail("'" + name + "': rank outside the world");
+  int me = -1;
+  kvm_comm* c = CommFor(ranks, &me);
+  if (me < 0 || !c) {
+    PlanStore(op->operands()[0], res);
+    return;
+  }
+  Buffer& out = Materialize(res);
+  void* dst = out.ptr;
+  const int P = int(ranks.size());
+  if (name == "comm.all_reduce.sum" || name == "comm.all_reduce.max") {
+    if (out.numel() != count) Fail(name + ": result shape != operand shape");
+    const int red = name == "comm.all_reduce.sum" ? KVM_RED_SUM : KVM_RED_MAX;
+    steps_.push_back([=](cudaStream_t st) {
+      return kvm_sm100_all_reduce(c, src, dst, count, dt, red, st);
+    });
+  } else if (name == "comm.all_gather") {
+    if (out.numel() != count * P)
+      Fail("comm.all_gather: result must hold ranks x operand elements (dim 0 stacked)");
+    steps_.push_back([=](cudaStream_t st) {
+      return kvm_sm100_all_gather(c, src, dst, count, dt, st);
+    });
+  } else if (name == "comm.all_to_all") {
+    if (out.numel() != count || count % P)
+      Fail("comm.all_to_all: operand must split evenly over the ranks (dim 0)");
+    steps_.push_back([=](cudaStream_t st) {
+      return kvm_sm100_all_to_all(c, src, dst, count / P, dt, st);
+    });
+  } else if (name == "comm.broadcast") {
+    if (out.numel() != count) Fail("comm.broadcast: result shape != operand shape");
+    const int root = int(std::find(ranks.begin(), ranks.end(), root_rank) - ranks.begin());
+    steps_.push_back([=](cudaStream_t st) {
+      return kvm_sm100_broadcast(c, src, dst, count, dt, root, st);
+    });
+  } else {
+    Fail("collective '" + name + "' is not supported");
+  }
+  std::string sn = name.substr(5);
+  std::replace(sn.begin(), sn.end(), '.', '_');
+  step_names_.push_back("comm_" + sn);
 }
 
 void Executor::CopyInput(int index, const void* host, int64_t bytes) {

@@ -25,12 +25,14 @@
 
 #include <cstdint>
 #include <functional>
+#include <map>
 #include <memory>
 #include <string>
 #include <unordered_map>
 #include <vector>
 
 #include "attr.h"
+#include "kvm_sm100.h"
 #include "dialect/dtype.h"
 #include "graph.h"
 
@@ -58,6 +60,11 @@ class Executor {
   // Block arguments, in order, with their shapes and dtypes.
   const std::vector<Buffer>& inputs() const { return inputs_; }
   const std::vector<std::string>& input_names() const { return input_names_; }
+
+  // Multi-process runs: the world communicator (kvm_sm100_comm_init) of this
+  // process's rank; the collectives of the graph run over it (and over
+  // communicators split from it for rank subsets). Set before Prepare.
+  void SetComm(kvm_comm* world);
 
   // Analysis and fusion only (no GPU needed); Prepare runs it first.
   void Plan();
@@ -130,6 +137,10 @@ class Executor {
   std::vector<std::string> fusions_;
   std::vector<std::function<int(cudaStream_t)>> once_steps_;  // weight re-layouts
   std::vector<std::function<int(cudaStream_t)>> steps_;
+  kvm_comm* world_ = nullptr;
+  int rank_ = 0, nranks_ = 1;
+  std::map<std::vector<int>, kvm_comm*> subcomms_;  // rank set -> communicator
+  kvm_comm* CommFor(const std::vector<int>& ranks, int* my_index);
   std::vector<std::string> step_names_;
   bool analyzed_ = false;
   bool prepared_ = false;

@@ -3,6 +3,7 @@
 //   kvm_run GRAPH.kvm [--inputs DIR] [--out DIR] [--seed S] [--warmup W]
 //                     [--iters N] [--dump-task] [--lower-only]
 //                     [--tile [--dump-tile]]
+//                     [--rank R --world N --comm-dir DIR]
 //   kvm_run --verify-tile TILE_GRAPH.kvm
 //
 // The graph is parsed by the reference parser (serial::Parse), lowered by the
@@ -15,11 +16,17 @@
 // --tile lowers the task graph further to the tile dialect (task_to_tile.h)
 // and checks every tile op against the sm_100a rules (no GPU needed);
 // --verify-tile checks a tile-dialect graph given as text.
+// --rank/--world run one rank of an N-process job (one process per GPU,
+// GPU R): rank 0 writes the NCCL unique id to DIR/nccl_id (the others wait
+// for it, 60 s at most; DIR starts empty), the graph's comm.* ops run over NCCL, inputs come
+// from <inputs>/r<R>/ and outputs go to <out>/r<R>/, and seeded inputs
+// use seed S + 1000003 R + argument index.
 #include <cuda_runtime.h>
 
 #include <any>
 #include <chrono>
 #include <cstdio>
+#include <thread>
 #include <cstring>
 #include <fstream>
 #include <iostream>
@@ -96,6 +103,39 @@ void Checksum(const kvm::sm100::Buffer& b, double* sum, double* sq) {
   }
 }
 
+// One rank joins an N-rank job on GPU `rank`: rank 0 makes the NCCL id and
+// publishes it by rename (readers never see a partial file).
+kvm_comm* JoinWorld(int rank, int world, const std::string& dir) {
+  int devices = 0;
+  cudaGetDeviceCount(&devices);
+  if (devices <= 0) throw std::runtime_error("no CUDA device");
+  cudaSetDevice(rank % devices);
+  std::vector<char> id(KVM_COMM_ID_BYTES);
+  const std::string path = dir + "/nccl_id";
+  if (rank == 0) {
+    if (kvm_sm100_comm_unique_id(id.data()) != KVM_OK)
+      throw std::runtime_error(std::string("comm id: ") + kvm_sm100_last_error());
+    const std::string tmp = path + ".tmp";
+    {
+      std::ofstream f(tmp, std::ios::binary);
+      f.write(id.data(), std::streamsize(id.size()));
+    }
+    if (std::rename(tmp.c_str(), path.c_str()) != 0)
+      throw std::runtime_error("cannot publish " + path);
+  } else {
+    std::vector<char> data;
+    for (int waited = 0; !ReadBin(path, data) || data.size() != id.size(); waited += 10) {
+      if (waited > 60000) throw std::runtime_error("rank 0 did not publish " + path);
+      std::this_thread::sleep_for(std::chrono::milliseconds(10));
+    }
+    id = data;
+  }
+  kvm_comm* c = nullptr;
+  if (kvm_sm100_comm_init(world, rank, id.data(), &c) != KVM_OK)
+    throw std::runtime_error(std::string("comm init: ") + kvm_sm100_last_error());
+  return c;
+}
+
 }  // namespace
 
 int main(int argc, char** argv) {
@@ -103,7 +143,8 @@ int main(int argc, char** argv) {
   uint64_t seed = 0;
   int warmup = 1, iters = 1;
   bool dump_task = false, lower_only = false, tile = false, dump_tile = false;
-  std::string verify_tile;
+  std::string verify_tile, comm_dir;
+  int rank = 0, world = 1;
   for (int i = 1; i < argc; ++i) {
     std::string a = argv[i];
     auto next = [&]() -> std::string {
@@ -120,6 +161,9 @@ int main(int argc, char** argv) {
     else if (a == "--tile") tile = true;
     else if (a == "--dump-tile") dump_tile = true;
     else if (a == "--verify-tile") verify_tile = next();
+    else if (a == "--rank") rank = std::stoi(next());
+    else if (a == "--world") world = std::stoi(next());
+    else if (a == "--comm-dir") comm_dir = next();
     else if (graph_path.empty()) graph_path = a;
     else throw std::runtime_error("unexpected argument " + a);
   }
@@ -154,7 +198,19 @@ int main(int argc, char** argv) {
     kvm::ir::kernel::RegisterKernelDialect(reg);
     kvm::ir::Graph kernel;
     kvm::ir::AttrMap attrs = kvm::ir::serial::Parse(ReadFile(graph_path), reg, kernel);
+    kvm_comm* comm = nullptr;
+    if (world > 1 && !tile && !lower_only) {
+      if (rank < 0 || rank >= world) throw std::runtime_error("--rank outside --world");
+      if (comm_dir.empty()) throw std::runtime_error("--world > 1 needs --comm-dir");
+      comm = JoinWorld(rank, world, comm_dir);  // selects GPU `rank` first
+    }
     kvm::sm100::Executor ex(kernel, attrs);
+    if (comm) {
+      ex.SetComm(comm);
+      if (!in_dir.empty()) in_dir += "/r" + std::to_string(rank);
+      if (!out_dir.empty()) out_dir += "/r" + std::to_string(rank);
+      seed += 1000003ull * uint64_t(rank);
+    }
     if (dump_task) {
       kvm::ir::serial::Registry treg;
       kvm::ir::task::RegisterTaskDialect(treg);
@@ -271,6 +327,7 @@ int main(int argc, char** argv) {
     js << "]}";
     std::cout << js.str() << std::endl;
     cudaStreamDestroy(st);
+    if (comm) kvm_sm100_comm_destroy(comm);
   } catch (const std::exception& e) {
     std::cerr << "kvm_run: " << e.what() << std::endl;
     return 1;
