@@ -55,14 +55,16 @@ def parse_args(argv=None):
                          "values are profiling cases, not bench lines)")
     ap.add_argument("--experts", type=int, default=EXPERTS,
                     help="experts (default 64; profiling cases may use fewer)")
-    ap.add_argument("--workload", choices=["moe", "gemm", "mlp", "fp8", "tp", "attn", "decode"],
+    ap.add_argument("--workload", choices=["moe", "gemm", "mlp", "fp8", "tp", "attn", "decode", "ew"],
                     default="moe",
                     help="moe (default, the headline line); gemm: bf16 1024^3 matmul; "
                          "mlp: gated MLP block 4096x4096->14336; fp8: W8A8 block-scaled "
                          "GEMM [M,8192]x[8192,28672] for M in 16,128,1024; tp: "
                          "tensor-parallel decoder layer (hidden 8192, batch 4 x 2048); "
                          "attn: the decoder layer's fused causal attention alone; "
-                         "decode: paged decode attention, --seqs sequences x 4096 keys")
+                         "decode: paged decode attention, --seqs sequences x 4096 keys; "
+                         "ew: generated fused elementwise programs (SiLU-gate, RMSNorm "
+                         "scaling) vs the interpreter")
     ap.add_argument("--seqs", type=int, default=64,
                     help="decode workload: sequences per step (64; smaller values are "
                          "profiling cases)")

@@ -453,6 +453,15 @@ typedef struct kvm_ew_inputs {
 int kvm_sm100_elementwise(const kvm_ew_program* program,
                           const kvm_ew_inputs* inputs, void* out, int64_t n,
                           kvm_stream_t stream);
+/* The program runs as a kernel generated for it (straight-line code, 8
+ * outputs per thread with 16-byte accesses when n % 8 == 0, pointers are
+ * 16-byte aligned and contiguous inputs have in_size % 8 == 0), compiled by
+ * NVRTC for sm_100a on the first call with that program and those sizes and
+ * cached for the process. kvm_sm100_elementwise_prepare does that compile
+ * ahead (no GPU needed; call it before capturing a stream that launches the
+ * program). Without libnvrtc.so.12 both return KVM_ERR_UNSUPPORTED. */
+int kvm_sm100_elementwise_prepare(const kvm_ew_program* program,
+                                  const kvm_ew_inputs* inputs, const void* out, int64_t n);
 
 /* y[m] = sum_k A[m, k] * x[k] (fp32 accumulation), y of out_dtype (KVM_BF16 /
  * KVM_F32): kernel.matmul with a [K, 1] right operand (e.g. the row means of

@@ -84,6 +84,7 @@ SIGNATURES = {
                                               _I, _I, _I, _F, _P, _I64, _P]),
     "kvm_sm100_rope_bf16": (_I, [_P, _I64, _I, _I, _I, _I, _F, _P]),
     "kvm_sm100_elementwise": (_I, [_P, _P, _P, _I64, _P]),
+    "kvm_sm100_elementwise_prepare": (_I, [_P, _P, _P, _I64]),
     "kvm_sm100_gemv_bf16": (_I, [_P, _I64, _P, _P, _I, _I, _I, _P]),
     "kvm_sm100_moe_topk": (_I, [_P, _I, _I, _I, _I, _P, _P, _P]),
     "kvm_sm100_fill_normal": (_I, [_P, _I, _I64, C.c_uint64, _F, _F, _P]),
@@ -125,6 +126,67 @@ class KvLayout(C.Structure):
                 ("kv_stride", C.c_int64), ("token_stride", C.c_int64),
                 ("block_size", C.c_int32), ("layer", C.c_int32), ("width", C.c_int32),
                 ("num_pages", C.c_int32)]
+
+
+KVM_EW_MAX_INPUTS, KVM_EW_MAX_INSTR, KVM_EW_MAX_REGS = 8, 32, 16
+# enum kvm_ew_dtype / kvm_ew_op (include/kvm_sm100.h)
+EW_DTYPES = {"bf16": 0, "f32": 1, "f16": 2, "i32": 3}
+EW_OPS = ["load", "add", "sub", "mul", "div", "max", "min", "neg", "exp", "log", "sqrt",
+          "rsqrt", "abs", "rcp", "cmp.eq", "cmp.ne", "cmp.lt", "cmp.le", "cmp.gt",
+          "cmp.ge", "round.bf16", "round.f16", "trunc.i32"]
+
+
+class EwProgram(C.Structure):
+    """Mirror of struct kvm_ew_program (include/kvm_sm100.h)."""
+    _fields_ = [("n_inputs", C.c_int32), ("n_instr", C.c_int32), ("out_reg", C.c_int32),
+                ("out_dtype", C.c_int32), ("in_dtype", C.c_int32 * KVM_EW_MAX_INPUTS),
+                ("in_size", C.c_int64 * KVM_EW_MAX_INPUTS),
+                ("in_div", C.c_int64 * KVM_EW_MAX_INPUTS),
+                ("op", C.c_uint8 * KVM_EW_MAX_INSTR), ("a", C.c_uint8 * KVM_EW_MAX_INSTR),
+                ("b", C.c_uint8 * KVM_EW_MAX_INSTR), ("dst", C.c_uint8 * KVM_EW_MAX_INSTR)]
+
+
+class EwInputs(C.Structure):
+    """Mirror of struct kvm_ew_inputs (include/kvm_sm100.h)."""
+    _fields_ = [("ptr", C.c_void_p * KVM_EW_MAX_INPUTS)]
+
+
+def broadcast_of(in_shape, out_shape) -> tuple[int, int]:
+    """(in_size, in_div) of an input of `in_shape` broadcast numpy-style to
+    `out_shape`: its non-1 dimensions, right-aligned, must be one contiguous
+    run of the output's dimensions."""
+    r = len(out_shape)
+    if len(in_shape) > r:
+        raise ValueError("elementwise operand has more dimensions than the result")
+    s = [1] * (r - len(in_shape)) + list(in_shape)
+    run = [d for d in range(r) if s[d] != 1]
+    for d in run:
+        if s[d] != out_shape[d]:
+            raise ValueError("elementwise operand does not broadcast")
+    if run and run != list(range(run[0], run[-1] + 1)):
+        raise ValueError("unsupported broadcast pattern")
+    if not run:
+        return 1, 1
+    size = 1
+    for d in run:
+        size *= out_shape[d]
+    div = 1
+    for d in range(run[-1] + 1, r):
+        div *= out_shape[d]
+    return size, div
+
+
+def ew_program(instrs, in_dtypes, in_bcast, out_dtype: str, out_reg: int) -> EwProgram:
+    """An EwProgram from (op, a, b, dst) tuples (op a name of EW_OPS; for
+    "load", `a` is the input slot), input dtype names and (size, div) pairs."""
+    p = EwProgram()
+    p.n_inputs, p.n_instr = len(in_dtypes), len(instrs)
+    p.out_reg, p.out_dtype = out_reg, EW_DTYPES[out_dtype]
+    for i, (dt, (size, div)) in enumerate(zip(in_dtypes, in_bcast)):
+        p.in_dtype[i], p.in_size[i], p.in_div[i] = EW_DTYPES[dt], size, div
+    for s, (op, a, b, dst) in enumerate(instrs):
+        p.op[s], p.a[s], p.b[s], p.dst[s] = EW_OPS.index(op), a, b, dst
+    return p
 
 
 _lib: C.CDLL | None = None

@@ -233,6 +233,60 @@ def run_decode(args, peaks, ClockSampler, dev, g) -> int:
     return 0
 
 
+SILU_PROGRAM = [("load", 0, 0, 0), ("load", 1, 0, 1), ("neg", 0, 0, 2), ("exp", 2, 0, 3),
+                ("load", 2, 0, 4), ("add", 3, 4, 5), ("div", 0, 5, 6), ("mul", 6, 1, 7)]
+NORM_PROGRAM = [("load", 0, 0, 0), ("load", 1, 0, 1), ("mul", 0, 1, 2), ("load", 2, 0, 3),
+                ("mul", 2, 3, 4)]
+
+
+def run_ew(args, peaks, ClockSampler, dev, g) -> int:
+    """Generic fused elementwise programs (kernels generated per program):
+    SiLU(g) * u over [8192, 14336] bf16 (the MoE/MLP gate shape) and the
+    RMSNorm scaling x * r[T, 1] * gamma[H] over [8192, 4096]; the interpreter
+    kernel (KVM_SM100_EW_JIT=0) timed beside it."""
+    import os
+    T, F, H = 8192, 14336, 4096
+    gt = torch.randn((T, F), generator=g, device=dev).to(torch.bfloat16)
+    ut = torch.randn((T, F), generator=g, device=dev).to(torch.bfloat16)
+    one = torch.ones((), dtype=torch.float32, device=dev)
+    ht = torch.empty((T, F), dtype=torch.bfloat16, device=dev)
+    x = torch.randn((T, H), generator=g, device=dev).to(torch.bfloat16)
+    r = torch.rand((T, 1), generator=g, device=dev)
+    gamma = torch.randn((H,), generator=g, device=dev).to(torch.bfloat16)
+    y = torch.empty_like(x)
+    steps, warmup = args.steps, max(args.warmup, 3)
+    scratch = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    silu = lambda: ops.elementwise(SILU_PROGRAM, [gt, ut, one], (T, F), out=ht)
+    norm = lambda: ops.elementwise(NORM_PROGRAM, [x, r, gamma], (T, H), out=y)
+    with ClockSampler(0) as ck:
+        t0 = time.time()
+        ms = _time(silu, steps, warmup)
+        t1 = time.time()
+    ms_norm = _time(norm, steps, warmup, flush=lambda: scratch.fill_(1))
+    os.environ["KVM_SM100_EW_JIT"] = "0"
+    try:
+        ms_i = _time(silu, max(steps // 4, 3), warmup)
+        ms_norm_i = _time(norm, max(steps // 4, 3), warmup, flush=lambda: scratch.fill_(1))
+    finally:
+        del os.environ["KVM_SM100_EW_JIT"]
+    byt = 3 * 2 * T * F
+    gbs = byt / (ms / 1e3) / 1e9
+    norm_bytes = 2 * 2 * T * H + 4 * T + 2 * H
+    _line(args, ck, t0, t1, metric="fused elementwise GB/s", value=gbs, unit="GB/s",
+          ms_per_step=ms, dtype="f32 registers, bf16 in/out",
+          config={"workload": f"silu_gate_program_{T}x{F}_bf16",
+                  "bytes_per_step": byt, "l2": f"{byt / 1e9:.2f} GB per step > L2",
+                  "interpreter_ms": ms_i,
+                  "rmsnorm_scale_program": {"shape": [T, H], "ms": ms_norm,
+                                            "gbs": norm_bytes / (ms_norm / 1e3) / 1e9,
+                                            "interpreter_ms": ms_norm_i,
+                                            "l2": "flushed before each launch"}},
+          roofline={"bound": "hbm", "achieved": gbs, "peak": peaks["hbm"], "unit": "GB/s",
+                    "frac": gbs / peaks["hbm"], "traffic": None, "kernel": "kvm_ew (generated)"},
+          gpu_launches=steps)
+    return 0
+
+
 def run(args, peaks, ClockSampler) -> int:
     if args.workload == "tp":
         return run_tp(args, peaks, ClockSampler)
@@ -262,6 +316,8 @@ def run(args, peaks, ClockSampler) -> int:
         return 0
     if args.workload == "decode":
         return run_decode(args, peaks, ClockSampler, dev, g)
+    if args.workload == "ew":
+        return run_ew(args, peaks, ClockSampler, dev, g)
     if args.workload == "attn":
         return run_attn(args, peaks, ClockSampler, dev, g)
     if args.workload == "mlp":

@@ -3,11 +3,14 @@
 //     (kernel.comm.moe_dispatch(x, g) with g an arbitrary tensor),
 //   * a generic elementwise interpreter for the kernel dialect's arithmetic,
 //     compare and cast ops (src/ir/dialect/kernel/dialect.cpp:43-55) with
-//     trailing-dimension broadcasting,
+//     trailing-dimension broadcasting (the reference semantics for the
+//     generated kernels of ew_jit.cu, and their A/B partner:
+//     KVM_SM100_EW_JIT=0 selects it),
 //   * a seeded normal fill for graph inputs.
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
+#include "ew_jit.h"
 #include "runtime.h"
 
 namespace kvm {
@@ -182,14 +185,16 @@ int grid_of(long long n, int sms) {
 
 using namespace kvm;
 
-extern "C" int kvm_sm100_elementwise(const kvm_ew_program* prog,
-                                     const kvm_ew_inputs* inputs, void* out,
-                                     int64_t n, kvm_stream_t stream) {
+namespace {
+
+int check_program(const kvm_ew_program* prog, const kvm_ew_inputs* inputs, const void* out,
+                  int64_t n) {
   if (!prog || !inputs || !out || n <= 0)
     return fail(KVM_ERR_INVALID_ARG, "elementwise: NULL argument or n <= 0");
   if (prog->n_instr < 1 || prog->n_instr > KVM_EW_MAX_INSTR || prog->n_inputs < 0 ||
       prog->n_inputs > KVM_EW_MAX_INPUTS || prog->out_reg < 0 ||
-      prog->out_reg >= KVM_EW_MAX_REGS)
+      prog->out_reg >= KVM_EW_MAX_REGS || prog->out_dtype < KVM_EW_BF16 ||
+      prog->out_dtype > KVM_EW_I32)
     return fail(KVM_ERR_INVALID_ARG, "elementwise: program out of bounds");
   for (int s = 0; s < prog->n_instr; ++s) {
     const int op = prog->op[s];
@@ -202,17 +207,38 @@ extern "C" int kvm_sm100_elementwise(const kvm_ew_program* prog,
       return fail(KVM_ERR_INVALID_ARG, "elementwise: register out of range");
     }
   }
-  for (int i = 0; i < prog->n_inputs; ++i)
+  for (int i = 0; i < prog->n_inputs; ++i) {
     if (!inputs->ptr[i] || prog->in_size[i] <= 0 || prog->in_div[i] <= 0 ||
         n % (prog->in_size[i] * prog->in_div[i]) != 0)
       return fail(KVM_ERR_INVALID_ARG,
                   "elementwise: each input's size x divisor must divide the output size");
+    if (prog->in_dtype[i] < KVM_EW_BF16 || prog->in_dtype[i] > KVM_EW_I32)
+      return fail(KVM_ERR_INVALID_ARG, "elementwise: bad input dtype");
+  }
+  return KVM_OK;
+}
+
+}  // namespace
+
+extern "C" int kvm_sm100_elementwise(const kvm_ew_program* prog,
+                                     const kvm_ew_inputs* inputs, void* out,
+                                     int64_t n, kvm_stream_t stream) {
+  if (int rc = check_program(prog, inputs, out, n); rc != KVM_OK) return rc;
+  if (ew_jit_enabled())
+    return ew_jit_launch(*prog, *inputs, out, n, static_cast<cudaStream_t>(stream));
   const DeviceInfo* dev = device_info();
   if (!dev) return KVM_ERR_CUDA;
   elementwise_kernel<<<grid_of(n, dev->sm_count), 256, 0,
                        static_cast<cudaStream_t>(stream)>>>(*prog, *inputs, out, n);
   KVM_CUDA_TRY(cudaGetLastError());
   return KVM_OK;
+}
+
+extern "C" int kvm_sm100_elementwise_prepare(const kvm_ew_program* prog,
+                                             const kvm_ew_inputs* inputs, const void* out,
+                                             int64_t n) {
+  if (int rc = check_program(prog, inputs, out, n); rc != KVM_OK) return rc;
+  return ew_jit_enabled() ? ew_jit_prepare(*prog, *inputs, out, n) : KVM_OK;
 }
 
 extern "C" int kvm_sm100_gemv_bf16(const void* A, int64_t lda, const void* x, void* y,

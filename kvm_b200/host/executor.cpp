@@ -752,6 +752,10 @@ void Executor::PlanExpr(const ir::ValueNode* expr, const Buffer& out) {
   for (int i = 0; i < prog.n_inputs; ++i)
     if (n % (prog.in_size[i] * prog.in_div[i]) != 0)
       Fail("elementwise operand does not broadcast to the result shape");
+  // generate + compile the fused kernel now, not inside the first (maybe
+  // captured) run
+  if (kvm_sm100_elementwise_prepare(&prog, &ins, d, n) != KVM_OK)
+    Fail(std::string("elementwise: ") + kvm_sm100_last_error());
   steps_.push_back([prog, ins, d, n](cudaStream_t st) {
     return kvm_sm100_elementwise(&prog, &ins, d, n, st);
   });

@@ -383,6 +383,43 @@ def moe_combine(y: torch.Tensor, pos: torch.Tensor, topk_w: torch.Tensor,
     return out
 
 
+# ----------------------------------------------------------- elementwise ---
+
+_EW_TORCH = {torch.bfloat16: "bf16", torch.float32: "f32", torch.float16: "f16",
+             torch.int32: "i32"}
+
+
+def elementwise(instrs, inputs, out_shape, out_dtype: torch.dtype = torch.bfloat16,
+                out_reg: int | None = None, out: torch.Tensor | None = None) -> torch.Tensor:
+    """out = program(inputs): a fused chain of the kernel dialect's elementwise
+    ops (kernel/dialect.cpp:43-55) as one generated sm_100a kernel.
+
+    instrs: (op, a, b, dst) tuples over 16 fp32 registers, op one of
+    _lib.EW_OPS ("load" reads input slot `a`); inputs: contiguous CUDA tensors
+    (bf16/f32/f16/i32) broadcast numpy-style to out_shape; the result is
+    register `out_reg` (default: the last instruction's dst) rounded to
+    out_dtype.
+    """
+    out_shape = tuple(int(d) for d in out_shape)
+    for i, t in enumerate(inputs):
+        if not t.is_cuda or not t.is_contiguous() or t.dtype not in _EW_TORCH:
+            raise ValueError(f"input {i} must be a contiguous CUDA bf16/f32/f16/i32 tensor")
+    if out is None:
+        out = torch.empty(out_shape, dtype=out_dtype, device=inputs[0].device if inputs
+                          else torch.device("cuda"))
+    prog = _lib.ew_program(instrs, [_EW_TORCH[t.dtype] for t in inputs],
+                           [_lib.broadcast_of(tuple(t.shape), out_shape) for t in inputs],
+                           _EW_TORCH[out.dtype],
+                           instrs[-1][3] if out_reg is None else out_reg)
+    ins = _lib.EwInputs()
+    for i, t in enumerate(inputs):
+        ins.ptr[i] = t.data_ptr()
+    import ctypes
+    call("kvm_sm100_elementwise", ctypes.byref(prog), ctypes.byref(ins), out.data_ptr(),
+         out.numel(), _stream())
+    return out
+
+
 def device_status() -> int:
     """Synchronise; raise KvmError if a kernel recorded a timeout or bad index."""
     return _lib.device_status(clear=True)
@@ -392,5 +429,5 @@ __all__ = [
     "matmul", "gemm", "pack_gate_up", "quantize_e4m3", "matmul_fp8", "transpose_u8",
     "transpose_f32", "attention_prefill", "rope_", "transpose", "silu_gate_matmul", "rmsnorm",
     "silu_mul", "moe_route", "moe_permute", "moe_scatter_rows", "grouped_matmul",
-    "moe_combine", "Routing", "Dispatch", "device_status", "KVM_B_KN", "KVM_B_NK",
+    "moe_combine", "Routing", "Dispatch", "elementwise", "device_status", "KVM_B_KN", "KVM_B_NK",
 ]

@@ -97,6 +97,60 @@ def bf16_to_f32(h: np.ndarray) -> np.ndarray:
     return (h.astype(np.uint32) << 16).view(np.float32)
 
 
+def elementwise(instrs, inputs, bcast, out_dtype: str, out_reg: int, n: int) -> np.ndarray:
+    """The elementwise program of kvm_sm100_elementwise, element by element in
+    fp32 numpy: the kernel dialect's arithmetic, compare and cast ops
+    (src/ir/dialect/kernel/dialect.cpp:43-55) as task.alu.* / task.sfu.*
+    (src/ir/dialect/task/dialect.cpp:36-51), each rounded to fp32 on its own.
+
+    instrs: (op, a, b, dst) tuples; inputs: (array, dtype name) with bf16 and
+    f16 as raw uint16 bits; bcast: (size, div) per input -- output element i
+    reads input[(i // div) % size]. Returns bf16/f16 as uint16 bits, f32 or
+    int32 (saturating toward zero, NaN -> 0)."""
+    i = np.arange(n, dtype=np.int64)
+    regs = [np.zeros(n, np.float32) for _ in range(16)]
+    f32 = np.float32
+    with np.errstate(all="ignore"):
+        for op, a, b, dst in instrs:
+            if op == "load":
+                arr, dt = inputs[a]
+                size, div = bcast[a]
+                flat = np.ascontiguousarray(arr).reshape(-1)
+                if dt == "bf16":
+                    vals = bf16_to_f32(flat)
+                elif dt == "f16":
+                    vals = flat.view(np.float16).astype(f32)
+                else:
+                    vals = flat.astype(f32)
+                v = vals[(i // div) % size]
+            else:
+                x, y = regs[a], regs[b]
+                v = {
+                    "add": lambda: x + y, "sub": lambda: x - y, "mul": lambda: x * y,
+                    "div": lambda: x / y, "max": lambda: np.fmax(x, y),
+                    "min": lambda: np.fmin(x, y), "neg": lambda: -x,
+                    "exp": lambda: np.exp(x), "log": lambda: np.log(x),
+                    "sqrt": lambda: np.sqrt(x), "rsqrt": lambda: f32(1) / np.sqrt(x),
+                    "abs": lambda: np.abs(x), "rcp": lambda: f32(1) / x,
+                    "cmp.eq": lambda: (x == y).astype(f32), "cmp.ne": lambda: (x != y).astype(f32),
+                    "cmp.lt": lambda: (x < y).astype(f32), "cmp.le": lambda: (x <= y).astype(f32),
+                    "cmp.gt": lambda: (x > y).astype(f32), "cmp.ge": lambda: (x >= y).astype(f32),
+                    "round.bf16": lambda: bf16_to_f32(f32_to_bf16(x)),
+                    "round.f16": lambda: x.astype(np.float16).astype(f32),
+                    "trunc.i32": lambda: np.trunc(x),
+                }[op]()
+            regs[dst] = np.asarray(v, dtype=f32)
+        r = regs[out_reg]
+        if out_dtype == "bf16":
+            return f32_to_bf16(r)
+        if out_dtype == "f16":
+            return r.astype(np.float16).view(np.uint16)
+        if out_dtype == "i32":
+            t = np.nan_to_num(np.trunc(r.astype(np.float64)), nan=0.0)
+            return np.clip(t, -2.0 ** 31, 2.0 ** 31 - 1).astype(np.int32)
+        return r
+
+
 def normal_bf16(rng: np.random.Generator, shape, std: float = 1.0) -> np.ndarray:
     """Seeded N(0, std^2) values rounded to bf16 (uint16 bits)."""
     return f32_to_bf16(rng.standard_normal(shape, dtype=np.float32) * np.float32(std))
