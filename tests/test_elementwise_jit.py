@@ -96,14 +96,15 @@ def test_oracle_silu_program():
 
 def _torch_in(arr, dt, cuda):
     import torch
+    arr = np.array(arr, copy=True)  # numpy scalars become 0-d arrays
     if dt in ("bf16", "f16"):
-        t = torch.from_numpy(np.ascontiguousarray(arr).view(np.int16)).to(cuda)
+        t = torch.from_numpy(arr.view(np.int16)).to(cuda)
         return t.view(torch.bfloat16 if dt == "bf16" else torch.float16)
     return torch.from_numpy(arr).to(cuda)
 
 
 def _rand_input(rng, dt, shape):
-    x = rng.standard_normal(shape).astype(np.float32) * 2
+    x = (np.asarray(rng.standard_normal(shape), dtype=np.float32) * 2).reshape(shape)
     if dt == "bf16":
         return oracle.f32_to_bf16(x)
     if dt == "f16":
