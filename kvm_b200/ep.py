@@ -298,13 +298,15 @@ class ExpertParallelMoE:
         if world > 1:
             dist.barrier(group=group)
 
-    def __call__(self, x, probe=None):
+    def __call__(self, x, probe=None, out=None):
         from ._lib import call
+        from .moe import _out_buffer
         T, H = x.shape
         if H != self.H or T > self.max_tokens or T <= 0:
             raise ValueError(f"x must be [T <= {self.max_tokens}, {self.H}]")
         if x.dtype != torch.bfloat16 or not x.is_cuda or not x.is_contiguous():
             raise ValueError("x must be a contiguous bf16 CUDA tensor")
+        dst = _out_buffer(out, self.out, T, H)
         self.epoch += 1
         ep, pr = self.epoch, self._peers_ref
         st = torch.cuda.current_stream().cuda_stream
@@ -333,8 +335,8 @@ class ExpertParallelMoE:
         call("kvm_sm100_ep_wait", pr, 2, ep, st)
         call("kvm_sm100_ep_combine", pr, self.idx.data_ptr(), self.pos.data_ptr(),
              self.offsets.data_ptr(), self.send_base.data_ptr(), self.topw.data_ptr(),
-             self.out.data_ptr(), T, self.cap, st)
-        return self.out[:T]
+             dst.data_ptr(), T, self.cap, st)
+        return dst[:T]
 
     def close(self):
         """Unmap peer buffers and free this rank's (collective: all ranks call it)."""

@@ -22,6 +22,15 @@ from . import ops
 from ._lib import call, lib
 
 
+def _out_buffer(out, own, T, H):
+    if out is None:
+        return own
+    if (out.dtype != torch.bfloat16 or not out.is_cuda or not out.is_contiguous()
+            or out.dim() != 2 or out.shape[0] < T or out.shape[1] != H):
+        raise ValueError(f"out must be a contiguous bf16 CUDA tensor [>= {T}, {H}]")
+    return out
+
+
 class MoELayer:
     """Top-k MoE layer with gated (SiLU) experts: H -> F -> H per expert.
 
@@ -83,9 +92,12 @@ class MoELayer:
         n = self._n * self.k
         return ops.Dispatch(self.offsets, self.pos[:n], self.src_token[:n])
 
-    def __call__(self, x: torch.Tensor, probe=None) -> torch.Tensor:
+    def __call__(self, x: torch.Tensor, probe=None, out: torch.Tensor | None = None
+                 ) -> torch.Tensor:
         """Run the layer on x [T, H]; `probe` = (start, end) CUDA events to
-        record around the gate/up grouped GEMM (for per-kernel timing)."""
+        record around the gate/up grouped GEMM (for per-kernel timing); `out`
+        (contiguous bf16 [>= T, H]) receives the result instead of the layer's
+        own buffer."""
         T, H = x.shape
         if H != self.H or T > self.max_tokens or T <= 0:
             raise ValueError(f"x must be [T<= {self.max_tokens}, {self.H}]")
@@ -110,9 +122,10 @@ class MoELayer:
             probe[1].record()
         call("kvm_sm100_grouped_gemm_bf16", self.h.data_ptr(), self.w2.data_ptr(),
              self.y.data_ptr(), self.offsets.data_ptr(), E, T * k, H, F, 0, st)
+        dst = _out_buffer(out, self.out, T, H)
         call("kvm_sm100_moe_combine", self.y.data_ptr(), self.pos.data_ptr(),
-             self.topk_w.data_ptr(), self.out.data_ptr(), T, k, H, st)
-        return self.out[:T]
+             self.topk_w.data_ptr(), dst.data_ptr(), T, k, H, st)
+        return dst[:T]
 
     # Kernels one call launches (router 1, permute 3, scatter 1, GEMMs 2, combine 1).
     LAUNCHES_PER_CALL = 8

@@ -161,3 +161,31 @@ def test_moe_layer_end_to_end(cuda):
     g = oracle.bf16_to_f32(to_bits(out))[same]
     r = oracle.bf16_to_f32(ref)[same]
     assert rel_err(g, r) < 1e-2
+
+
+def test_host_pipeline_matches_layer(cuda):
+    """HostPipeline (pinned host batches, copies overlapped with compute on
+    three streams) returns, for every batch, exactly what the layer returns
+    for that batch on one stream -- including a ragged last batch and more
+    batches than device slots."""
+    from kvm_b200.moe import MoELayer
+    from kvm_b200.pipeline import HostPipeline
+    rng = np.random.default_rng(43)
+    T, H, E, F, k = 512, 512, 16, 256, 2
+    wr, w13, w2 = _weights(rng, E, H, F)
+    layer = MoELayer.from_packed(from_bits(wr, cuda), from_bits(w13, cuda),
+                                 from_bits(w2, cuda), top_k=k, max_tokens=T)
+    sizes = [512, 512, 300, 512, 7]
+    xs = [oracle.normal_bf16(rng, (n, H)) for n in sizes]
+    want = [to_bits(layer(from_bits(x, cuda)).clone()) for x in xs]
+    pipe = HostPipeline(layer, T, H, depth=2, device=cuda)
+    hin = [from_bits(x, "cpu").pin_memory() for x in xs]
+    hout = [torch.empty((n, H), dtype=torch.bfloat16).pin_memory() for n in sizes]
+    for a, b in zip(hin, hout):
+        pipe.submit(a, b)
+    pipe.synchronize()
+    ops.device_status()
+    for i, (w, o) in enumerate(zip(want, hout)):
+        assert np.array_equal(to_bits(o), w), i
+    with pytest.raises(ValueError):
+        pipe.submit(torch.empty((4, H), dtype=torch.bfloat16), hout[0][:4])
