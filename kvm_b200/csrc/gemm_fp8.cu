@@ -11,6 +11,7 @@
 // overlaps the promotion of block kb. Scales are arbitrary fp32 values, which
 // the tensor core's own block scaling (powers of two) cannot represent.
 #include <cuda_bf16.h>
+#include <cstdlib>
 #include <cuda_fp8.h>
 
 #include "ptx.cuh"
@@ -21,7 +22,9 @@ namespace {
 
 constexpr int kF8BM = 128;
 constexpr int kF8BK = 128;   // bytes == elements
-constexpr int kF8Threads = 320;  // producer, MMA, 8 epilogue warps
+// producer warp, MMA warp, EW epilogue warps (each TMEM lane quarter is read
+// by EW/4 warps, one column slice each)
+constexpr int f8_threads(int ew) { return 64 + 32 * ew; }
 
 struct Fp8Params {
   int M, N, K;
@@ -30,16 +33,31 @@ struct Fp8Params {
   __nv_bfloat16* D;
   long long ldd;
   int* status;
-  int splits;        // > 1: the K blocks of each tile are split over `splits`
-  float* partial;    //      work units; each writes an fp32 partial tile here
+  // Work split. stream_k: CTA c takes K blocks [c*W/G, (c+1)*W/G) of the
+  // tile-major sequence of all tiles' K blocks (W = tiles * K/128, G =
+  // gridDim.x), so every CTA gets the same number of blocks whatever the
+  // tile count. Only a CTA's first and last segments can be parts of a tile
+  // cut between CTAs; those are written as fp32 partials (slot 2c for the
+  // first, 2c + 1 for the last) and summed by fp8_streamk_reduce_kernel.
+  // Otherwise CTA c takes whole tiles c, c+G, ...
+  int stream_k;
+  float* partial;    // [G][2][128][128] fp32
 };
 
-template <int BN, int STAGES, int NBUF>
+// Operand tiles of one 128-deep K block. TN == 0: A = 128 activation rows,
+// B = 128 weight rows, D[act row][weight col] in TMEM lanes x columns.
+// TN > 0 (M <= TN <= 64): A = 128 weight rows, B = TN activation rows (the
+// token count as the MMA's N), D^T in TMEM (lane = weight row = output
+// column, column = token).
+template <int STAGES, int NBUF, int TN>
 struct Fp8Smem {
-  static constexpr uint32_t kABytes = kF8BM * kF8BK;
-  static constexpr uint32_t kBBytes = BN * kF8BK;
+  static constexpr uint32_t kABytes = 128 * kF8BK;
+  static constexpr uint32_t kBBytes = (TN ? TN : 128) * kF8BK;
   static constexpr uint32_t kStage = kABytes + kBBytes;
-  static constexpr uint32_t kTmemCols = NBUF * BN;
+  static constexpr uint32_t kAccCols = TN ? TN : 128;
+  static constexpr uint32_t kTmemCols =
+      NBUF * kAccCols <= 32 ? 32 : NBUF * kAccCols <= 64 ? 64 : NBUF * kAccCols <= 128
+          ? 128 : NBUF * kAccCols <= 256 ? 256 : 512;
   static constexpr size_t kTotal =
       1024 + static_cast<size_t>(STAGES) * kStage + (2 * STAGES + 2 * NBUF + 1) * 8 + 16;
 };
@@ -49,15 +67,46 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
-template <int BN, int STAGES, int NBUF>
-__global__ void __launch_bounds__(kF8Threads, 1)
+// The segments (tile, K blocks [kb0, kb1)) a CTA works through, in order.
+struct Fp8Segments {
+  long long x, hi;   // stream-K: next K-block index, end of this CTA's range
+  int t, tiles, step, kbs, stream_k;
+  __device__ Fp8Segments(const Fp8Params& p, int tiles_, int kbs_)
+      : tiles(tiles_), step(static_cast<int>(gridDim.x)), kbs(kbs_), stream_k(p.stream_k) {
+    const long long W = static_cast<long long>(tiles_) * kbs_;
+    x = W * blockIdx.x / gridDim.x;
+    hi = W * (blockIdx.x + 1) / gridDim.x;
+    t = static_cast<int>(blockIdx.x);
+  }
+  __device__ bool next(int& tile, int& kb0, int& kb1) {
+    if (stream_k) {
+      if (x >= hi) return false;
+      tile = static_cast<int>(x / kbs);
+      kb0 = static_cast<int>(x - static_cast<long long>(tile) * kbs);
+      kb1 = static_cast<int>(min(static_cast<long long>(kbs), kb0 + (hi - x)));
+      x += kb1 - kb0;
+      return true;
+    }
+    if (t >= tiles) return false;
+    tile = t;
+    kb0 = 0;
+    kb1 = kbs;
+    t += step;
+    return true;
+  }
+};
+
+template <int STAGES, int NBUF, int EW, int TN>
+__global__ void __launch_bounds__(f8_threads(EW), 1)
     gemm_fp8_bs_kernel(const __grid_constant__ CUtensorMap tmA,
                        const __grid_constant__ CUtensorMap tmB,
                        const Fp8Params p) {
-  using S = Fp8Smem<BN, STAGES, NBUF>;
-  static_assert(BN == 128, "scales assume one 128-column block per tile");
-  constexpr uint32_t kIdesc = idesc_e4m3(kF8BM, BN, 0, 0);
-  constexpr int HALF = BN / 2;
+  using S = Fp8Smem<STAGES, NBUF, TN>;
+  constexpr int BN = 128;
+  static_assert(TN == 0 ? EW == 8 : EW == 4, "8 epilogue warps, or 4 in the swapped form");
+  static_assert(TN % 16 == 0 && TN <= 64, "swapped form: N = 16, 32, 48 or 64 tokens");
+  constexpr uint32_t kIdesc = idesc_e4m3(128, TN ? TN : BN, 0, 0);
+  constexpr int COLS = TN ? TN : BN / (EW / 4);  // accumulator columns per thread
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
@@ -72,18 +121,10 @@ __global__ void __launch_bounds__(kF8Threads, 1)
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int m_tiles = (p.M + kF8BM - 1) / kF8BM;
-  const int n_tiles = p.N / BN;
-  const int splits = p.splits > 1 ? p.splits : 1;
-  const int total = m_tiles * n_tiles * splits;
+  const int tiles = m_tiles * (p.N / BN);
   const int kbs = p.K / kF8BK;
-  // unit t: tile t / splits (N-tile major), K blocks [kb0, kb1) of split t % splits
-  auto unit = [&](int t, int& nt, int& mt, int& kb0, int& kb1) {
-    const int tile = t / splits, sp = t - tile * splits;
-    nt = tile / m_tiles;
-    mt = tile - nt * m_tiles;
-    kb0 = static_cast<int>(static_cast<long long>(sp) * kbs / splits);
-    kb1 = static_cast<int>(static_cast<long long>(sp + 1) * kbs / splits);
-  };
+  // tile t: N tile t / m_tiles (weight-major, so the M tiles of one weight
+  // tile run back to back and share it in L2), M tile t % m_tiles
 
   if (threadIdx.x == 0) {
     *abort_flag = 0;
@@ -93,7 +134,7 @@ __global__ void __launch_bounds__(kF8Threads, 1)
     }
     for (int b = 0; b < NBUF; ++b) {
       mbar_init(&tfull[b], 1);
-      mbar_init(&tempty[b], 256);
+      mbar_init(&tempty[b], 32 * EW);
     }
     mbar_init(drain, 1);
     fence_mbar_init();
@@ -116,15 +157,21 @@ __global__ void __launch_bounds__(kF8Threads, 1)
       int s = 0;
       uint32_t ph = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
-        int nt, mt, kb0, kb1;
-        unit(t, nt, mt, kb0, kb1);
+      Fp8Segments seg(p, tiles, kbs);
+      int tile, kb0, kb1;
+      while (ok && seg.next(tile, kb0, kb1)) {
+        const int nt = tile / m_tiles, mt = tile - (tile / m_tiles) * m_tiles;
         for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&empty[s], ph ^ 1, abort_flag)) { ok = false; break; }
           uint8_t* a_dst = smem + s * S::kStage;
           mbar_arrive_expect_tx(&full[s], S::kStage);
-          tma_load_2d(a_dst, &tmA, &full[s], kb * kF8BK, mt * kF8BM);
-          tma_load_2d(a_dst + S::kABytes, &tmB, &full[s], kb * kF8BK, nt * BN);
+          if (TN) {  // A = weights, B = the (only) M tile of activations
+            tma_load_2d(a_dst, &tmB, &full[s], kb * kF8BK, nt * BN);
+            tma_load_2d(a_dst + S::kABytes, &tmA, &full[s], kb * kF8BK, 0);
+          } else {
+            tma_load_2d(a_dst, &tmA, &full[s], kb * kF8BK, mt * kF8BM);
+            tma_load_2d(a_dst + S::kABytes, &tmB, &full[s], kb * kF8BK, nt * BN);
+          }
           if (++s == STAGES) { s = 0; ph ^= 1; }
         }
       }
@@ -143,9 +190,9 @@ __global__ void __launch_bounds__(kF8Threads, 1)
       uint32_t ph = 0;
       uint32_t g = 0;  // K blocks issued so far (selects the TMEM buffer)
       bool ok = true;
-      for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
-        int nt, mt, kb0, kb1;
-        unit(t, nt, mt, kb0, kb1);
+      Fp8Segments seg(p, tiles, kbs);
+      int tile, kb0, kb1;
+      while (ok && seg.next(tile, kb0, kb1)) {
         for (int kb = kb0; kb < kb1; ++kb, ++g) {
           const uint32_t b = g % NBUF, bph = (g / NBUF) & 1;
           if (!mbar_wait(&tempty[b], bph ^ 1, abort_flag)) { ok = false; break; }
@@ -153,7 +200,7 @@ __global__ void __launch_bounds__(kF8Threads, 1)
           tc_fence_after();
           const uint32_t a_addr = smem_u32(smem + s * S::kStage);
           const uint32_t b_addr = a_addr + S::kABytes;
-          const uint32_t d = tmem_base + b * BN;
+          const uint32_t d = tmem_base + b * S::kAccCols;
 #pragma unroll
           for (int k = 0; k < kF8BK / 32; ++k)
             mma_f8_ss(d, sdesc_sw128(a_addr + k * 32, 0, 1024),
@@ -168,59 +215,91 @@ __global__ void __launch_bounds__(kF8Threads, 1)
       mbar_wait(drain, 0, &local_abort);
     }
   } else {
-    // epilogue: warp quarter q owns TMEM lanes [32q, 32q+32); half h owns
-    // columns [h*BN/2, (h+1)*BN/2).
+    // epilogue: warp quarter q owns TMEM lanes [32q, 32q+32); slice h owns
+    // accumulator columns [h*COLS, (h+1)*COLS).
     const int q = warp & 3, h = (warp - 2) >> 2;
-    const int r_in = q * 32 + lane;
+    const int r_in = q * 32 + lane;  // TMEM lane: activation row, or weight row if TN
     uint32_t g = 0;
     bool ok = true;
-    for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
-      int nt, mt, kb0, kb1;
-      unit(t, nt, mt, kb0, kb1);
-      const int row = mt * kF8BM + r_in;
-      float acc[HALF];
+    Fp8Segments seg(p, tiles, kbs);
+    int tile, kb0, kb1, si = 0;
+    while (ok && seg.next(tile, kb0, kb1)) {
+      const int nt = tile / m_tiles, mt = tile - nt * m_tiles;
+      float acc[COLS];
 #pragma unroll
-      for (int j = 0; j < HALF; ++j) acc[j] = 0.f;
+      for (int j = 0; j < COLS; ++j) acc[j] = 0.f;
       const float* sa = p.sA + static_cast<long long>(mt) * kbs;
       const float* sw = p.sW + static_cast<long long>(nt) * kbs;
+      // The tile's block scales s(kb) = sA * sW, 32 K blocks at a time: lane l
+      // loads block kb0 + 32c + l before the wait, a shuffle hands each block
+      // its scale (no global-load latency inside the loop).
+      float sc_lane = 0.f;
       for (int kb = kb0; kb < kb1; ++kb, ++g) {
+        const int j32 = (kb - kb0) & 31;
+        if (j32 == 0) {
+          const int kk = kb + lane;
+          sc_lane = kk < kb1 ? __ldg(sa + kk) * __ldg(sw + kk) : 0.f;
+        }
         const uint32_t b = g % NBUF, bph = (g / NBUF) & 1;
         const bool ready = mbar_wait(&tfull[b], bph, abort_flag);
         if (!__all_sync(0xffffffffu, ready)) { ok = false; break; }
         tc_fence_after();
         const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
-                               b * BN + h * HALF;
-        uint32_t v[HALF];
-        uint32_t (&v0)[32] = *reinterpret_cast<uint32_t(*)[32]>(&v[0]);
-        uint32_t (&v1)[32] = *reinterpret_cast<uint32_t(*)[32]>(&v[32]);
-        tmem_ld32(taddr, v0);
-        tmem_ld32(taddr + 32, v1);
+                               b * S::kAccCols + h * COLS;
+        uint32_t v[COLS];
+        if constexpr (COLS % 32 == 0) {
+#pragma unroll
+          for (int c = 0; c < COLS / 32; ++c)
+            tmem_ld32(taddr + 32 * c, *reinterpret_cast<uint32_t(*)[32]>(&v[32 * c]));
+        } else {
+#pragma unroll
+          for (int c = 0; c < COLS / 16; ++c)
+            tmem_ld16(taddr + 16 * c, *reinterpret_cast<uint32_t(*)[16]>(&v[16 * c]));
+        }
         tmem_wait_ld();
         tc_fence_before();
         mbar_arrive(&tempty[b]);
-        const float sc = __ldg(sa + kb) * __ldg(sw + kb);
+        const float sc = __shfl_sync(0xffffffffu, sc_lane, j32);
 #pragma unroll
-        for (int j = 0; j < HALF; ++j)
+        for (int j = 0; j < COLS; ++j)
           acc[j] = __fmaf_rn(__uint_as_float(v[j]), sc, acc[j]);
       }
       if (!ok) break;
-      if (splits > 1) {
-        if (row < p.M) {  // fp32 partial [unit][128 rows][BN], valid rows only
-          float4* dst = reinterpret_cast<float4*>(
-              p.partial + (static_cast<long long>(t) * kF8BM + r_in) * BN + h * HALF);
+      const bool whole = kb0 == 0 && kb1 == kbs;
+      float* part = whole ? nullptr
+                          : p.partial + (static_cast<long long>(blockIdx.x) * 2 + (si ? 1 : 0)) *
+                                            (kF8BM * BN);
+      ++si;
+      if (TN) {
+        // thread = output column nt*128 + r_in; acc[m] = token m (M <= TN)
+        const int col = nt * BN + r_in;
 #pragma unroll
-          for (int i = 0; i < HALF / 4; ++i)
-            dst[i] = make_float4(acc[4 * i], acc[4 * i + 1], acc[4 * i + 2], acc[4 * i + 3]);
+        for (int m = 0; m < COLS; ++m) {
+          if (m >= p.M) break;
+          if (whole)
+            p.D[static_cast<long long>(m) * p.ldd + col] = __float2bfloat16_rn(acc[m]);
+          else
+            part[m * BN + r_in] = acc[m];
         }
-      } else if (row < p.M) {
-        uint4* dst = reinterpret_cast<uint4*>(
-            p.D + static_cast<long long>(row) * p.ldd + nt * BN + h * HALF);
+      } else {
+        const int row = mt * kF8BM + r_in;
+        if (row < p.M) {
+          if (!whole) {  // fp32 partial [128 rows][128 cols], valid rows only
+            float4* dst = reinterpret_cast<float4*>(part + r_in * BN + h * COLS);
 #pragma unroll
-        for (int i = 0; i < HALF / 8; ++i)
-          dst[i] = make_uint4(pack_bf16x2(acc[8 * i], acc[8 * i + 1]),
-                              pack_bf16x2(acc[8 * i + 2], acc[8 * i + 3]),
-                              pack_bf16x2(acc[8 * i + 4], acc[8 * i + 5]),
-                              pack_bf16x2(acc[8 * i + 6], acc[8 * i + 7]));
+            for (int i = 0; i < COLS / 4; ++i)
+              dst[i] = make_float4(acc[4 * i], acc[4 * i + 1], acc[4 * i + 2], acc[4 * i + 3]);
+          } else {
+            uint4* dst = reinterpret_cast<uint4*>(
+                p.D + static_cast<long long>(row) * p.ldd + nt * BN + h * COLS);
+#pragma unroll
+            for (int i = 0; i < COLS / 8; ++i)
+              dst[i] = make_uint4(pack_bf16x2(acc[8 * i], acc[8 * i + 1]),
+                                  pack_bf16x2(acc[8 * i + 2], acc[8 * i + 3]),
+                                  pack_bf16x2(acc[8 * i + 4], acc[8 * i + 5]),
+                                  pack_bf16x2(acc[8 * i + 6], acc[8 * i + 7]));
+          }
+        }
       }
     }
   }
@@ -234,18 +313,31 @@ __global__ void __launch_bounds__(kF8Threads, 1)
   }
 }
 
-// Sum of the split partials in split order, to bf16: one thread per 8 outputs.
-__global__ void fp8_split_reduce_kernel(const float* __restrict__ partial,
-                                        __nv_bfloat16* __restrict__ D, long long ldd,
-                                        int M, int N, int m_tiles, int splits, int BN) {
+// The CTA whose stream-K range holds K-block index x (of W over G CTAs).
+__device__ __forceinline__ int streamk_cta(long long x, long long W, int G) {
+  return static_cast<int>(((x + 1) * G - 1) / W);
+}
+
+// Tiles cut between CTAs: sum the CTAs' fp32 partials in CTA order (= K
+// order), round to bf16. One thread per 8 outputs; tiles held whole by one
+// CTA were written by the GEMM and are skipped.
+__global__ void fp8_streamk_reduce_kernel(const float* __restrict__ partial,
+                                          __nv_bfloat16* __restrict__ D, long long ldd,
+                                          int M, int N, int kbs, int G) {
   const long long i = (blockIdx.x * 256ll + threadIdx.x) * 8;
   if (i >= static_cast<long long>(M) * N) return;
   const int row = static_cast<int>(i / N), col = static_cast<int>(i % N);
-  const int nt = col / BN, mt = row / kF8BM;
-  const long long tile = static_cast<long long>(nt) * m_tiles + mt;
+  const int m_tiles = (M + kF8BM - 1) / kF8BM;
+  const long long tile = static_cast<long long>(col / 128) * m_tiles + row / kF8BM;
+  const long long W = static_cast<long long>(m_tiles) * (N / 128) * kbs;
+  const int c_lo = streamk_cta(tile * kbs, W, G);
+  const int c_hi = streamk_cta(tile * kbs + kbs - 1, W, G);
+  if (c_lo == c_hi) return;
   float a[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-  for (int sp = 0; sp < splits; ++sp) {
-    const float* src = partial + ((tile * splits + sp) * kF8BM + row % kF8BM) * BN + col % BN;
+  for (int c = c_lo; c <= c_hi; ++c) {
+    const long long first = (W * c / G) / kbs;  // first tile of CTA c
+    const long long slot = static_cast<long long>(c) * 2 + (tile == first ? 0 : 1);
+    const float* src = partial + (slot * kF8BM + row % kF8BM) * 128 + col % 128;
     const float4 x = reinterpret_cast<const float4*>(src)[0];
     const float4 y = reinterpret_cast<const float4*>(src)[1];
     a[0] += x.x; a[1] += x.y; a[2] += x.z; a[3] += x.w;
@@ -256,23 +348,13 @@ __global__ void fp8_split_reduce_kernel(const float* __restrict__ partial,
                  pack_bf16x2(a[4], a[5]), pack_bf16x2(a[6], a[7]));
 }
 
-// K splits so that every SM gets a work unit when there are fewer output
-// tiles than SMs; with at least one tile per SM the partial traffic costs more
-// than the balance gains (measured at M = 16 and 128 with N = 28672).
-int choose_splits(int tiles, int kbs, int sms) {
-  if (tiles >= sms) return 1;
-  int best = 1;
-  double best_eff = 0.0;
-  for (int s = 1; s <= 8 && kbs / s >= 4; ++s) {
-    const long long units = static_cast<long long>(tiles) * s;
-    const long long waves = (units + sms - 1) / sms;
-    const double eff = static_cast<double>(units) / (waves * sms);
-    if (eff > best_eff + 0.02) {
-      best_eff = eff;
-      best = s;
-    }
-  }
-  return best;
+// Whether stream-K over `ctas` CTAs cuts any of `tiles` tiles of `kbs` K
+// blocks between two CTAs (then partials and a reduction are needed).
+bool streamk_cuts(long long tiles, int kbs, int ctas) {
+  const long long W = tiles * kbs;
+  for (int c = 1; c < ctas; ++c)
+    if ((W * c / ctas) % kbs != 0) return true;
+  return false;
 }
 
 // 128x128 block quantiser: one block of 256 threads per 128x128 tile.
@@ -356,13 +438,52 @@ __global__ void transpose_f32_kernel(const float* __restrict__ in,
 
 using namespace kvm;
 
+namespace kvm {
+namespace {
+
+// Launch geometry of one FP8 GEMM: the swapped form for M <= 64, stream-K
+// over min(SMs, K blocks) CTAs.
+struct Fp8Plan {
+  int tn;         // 0, or the swapped form's token tile (16, 32, 64)
+  int tiles, kbs, ctas;
+  bool cuts;          // stream-K cuts tiles: partials + reduction
+  int64_t workspace;  // bytes of fp32 partials stream-K needs (0: none)
+};
+
+Fp8Plan fp8_plan(int M, int N, int K, int sms) {
+  Fp8Plan pl;
+  pl.tn = M <= 16 ? 16 : M <= 32 ? 32 : M <= 64 ? 64 : 0;
+  pl.tiles = ((M + kF8BM - 1) / kF8BM) * (N / 128);
+  pl.kbs = K / kF8BK;
+  const long long W = static_cast<long long>(pl.tiles) * pl.kbs;
+  pl.ctas = static_cast<int>(W < sms ? W : sms);
+  pl.cuts = streamk_cuts(pl.tiles, pl.kbs, pl.ctas);
+  pl.workspace = pl.cuts ? static_cast<int64_t>(pl.ctas) * 2 * kF8BM * 128 * 4 : 0;
+  return pl;
+}
+
+template <int STAGES, int NBUF, int EW, int TN>
+int launch_fp8(const CUtensorMap& ta, const CUtensorMap& tb, const Fp8Params& p, int grid,
+               cudaStream_t stream) {
+  auto kern = gemm_fp8_bs_kernel<STAGES, NBUF, EW, TN>;
+  constexpr size_t smem = Fp8Smem<STAGES, NBUF, TN>::kTotal;
+  static_assert(smem <= 227 * 1024, "shared memory");
+  KVM_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    int(smem)));
+  kern<<<grid, f8_threads(EW), smem, stream>>>(ta, tb, p);
+  KVM_CUDA_TRY(cudaGetLastError());
+  return KVM_OK;
+}
+
+}  // namespace
+}  // namespace kvm
+
+using namespace kvm;
+
 extern "C" int64_t kvm_sm100_gemm_fp8_workspace(int M, int N, int K) {
   if (M <= 0 || N <= 0 || K <= 0 || K % 128 != 0 || N % 128 != 0) return 0;
   const DeviceInfo* dev = device_info();
-  const int sms = dev ? dev->sm_count : 148;
-  const int tiles = ((M + kF8BM - 1) / kF8BM) * (N / 128);
-  const int splits = choose_splits(tiles, K / kF8BK, sms);
-  return splits > 1 ? static_cast<int64_t>(tiles) * splits * kF8BM * 128 * 4 : 0;
+  return fp8_plan(M, N, K, dev ? dev->sm_count : 148).workspace;
 }
 
 extern "C" int kvm_sm100_gemm_fp8_blockscaled(const void* Aq, const float* sA,
@@ -371,8 +492,7 @@ extern "C" int kvm_sm100_gemm_fp8_blockscaled(const void* Aq, const float* sA,
                                               int N, int K, void* workspace,
                                               int64_t workspace_bytes,
                                               kvm_stream_t stream) {
-  constexpr int BN = 128, STAGES = 6, NBUF = 4;
-  if (M <= 0 || N <= 0 || K <= 0 || K % 128 != 0 || N % BN != 0)
+  if (M <= 0 || N <= 0 || K <= 0 || K % 128 != 0 || N % 128 != 0)
     return fail(KVM_ERR_INVALID_ARG,
                 "fp8 gemm: need M > 0, K % 128 == 0 and N % 128 == 0");
   if (!Aq || !Wq || !sA || !sW || !D || !aligned16(Aq) || !aligned16(Wq) ||
@@ -380,33 +500,34 @@ extern "C" int kvm_sm100_gemm_fp8_blockscaled(const void* Aq, const float* sA,
     return fail(KVM_ERR_INVALID_ARG, "fp8 gemm: NULL or unaligned operand");
   const DeviceInfo* dev = device_info();
   if (!dev) return KVM_ERR_CUDA;
-  CUtensorMap ta, tb;
-  KVM_TRY(encode_tmap_2d(&ta, Aq, K, M, K, kF8BK, kF8BM,
-                         CU_TENSOR_MAP_DATA_TYPE_UINT8, CU_TENSOR_MAP_SWIZZLE_128B));
-  KVM_TRY(encode_tmap_2d(&tb, Wq, K, N, K, kF8BK, BN,
-                         CU_TENSOR_MAP_DATA_TYPE_UINT8, CU_TENSOR_MAP_SWIZZLE_128B));
-  const int m_tiles = (M + kF8BM - 1) / kF8BM;
-  const int tiles = m_tiles * (N / BN);
-  int splits = choose_splits(tiles, K / kF8BK, dev->sm_count);
-  const int64_t need = static_cast<int64_t>(tiles) * splits * kF8BM * BN * 4;
-  if (splits > 1 && (!workspace || workspace_bytes < need || !aligned16(workspace)))
-    splits = 1;  // no room for partials: one unit per tile
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const Fp8Plan pl = fp8_plan(M, N, K, dev->sm_count);
+  // Stream-K needs room for the partials; without it each CTA takes whole
+  // tiles in turn.
+  const bool stream_k = !pl.cuts ||
+                        (workspace && workspace_bytes >= pl.workspace && aligned16(workspace));
   Fp8Params p{M, N, K, sA, sW, static_cast<__nv_bfloat16*>(D), ldd, dev->status,
-              splits, static_cast<float*>(workspace)};
-  const int units = tiles * splits;
-  const int grid = units < dev->sm_count ? units : dev->sm_count;
-  auto kern = gemm_fp8_bs_kernel<BN, STAGES, NBUF>;
-  constexpr size_t smem = Fp8Smem<BN, STAGES, NBUF>::kTotal;
-  KVM_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    int(smem)));
-  kern<<<grid, kF8Threads, smem, static_cast<cudaStream_t>(stream)>>>(ta, tb, p);
-  KVM_CUDA_TRY(cudaGetLastError());
-  if (splits > 1) {
+              stream_k ? 1 : 0, static_cast<float*>(workspace)};
+  const int grid = stream_k ? pl.ctas : (pl.tiles < dev->sm_count ? pl.tiles : dev->sm_count);
+  const int a_rows = pl.tn ? pl.tn : kF8BM;  // activation rows one TMA box holds
+  CUtensorMap ta, tb;
+  KVM_TRY(encode_tmap_2d(&ta, Aq, K, M, K, kF8BK, a_rows,
+                         CU_TENSOR_MAP_DATA_TYPE_UINT8, CU_TENSOR_MAP_SWIZZLE_128B));
+  KVM_TRY(encode_tmap_2d(&tb, Wq, K, N, K, kF8BK, 128,
+                         CU_TENSOR_MAP_DATA_TYPE_UINT8, CU_TENSOR_MAP_SWIZZLE_128B));
+  int rc;
+  switch (pl.tn) {
+    case 16: rc = launch_fp8<11, 8, 4, 16>(ta, tb, p, grid, st); break;
+    case 32: rc = launch_fp8<10, 8, 4, 32>(ta, tb, p, grid, st); break;
+    case 64: rc = launch_fp8<8, 4, 4, 64>(ta, tb, p, grid, st); break;
+    default: rc = launch_fp8<6, 4, 8, 0>(ta, tb, p, grid, st); break;
+  }
+  if (rc != KVM_OK) return rc;
+  if (stream_k && pl.cuts) {
     const long long n8 = (static_cast<long long>(M) * N) / 8;
-    fp8_split_reduce_kernel<<<static_cast<unsigned>((n8 + 255) / 256), 256, 0,
-                              static_cast<cudaStream_t>(stream)>>>(
+    fp8_streamk_reduce_kernel<<<static_cast<unsigned>((n8 + 255) / 256), 256, 0, st>>>(
         static_cast<const float*>(workspace), static_cast<__nv_bfloat16*>(D), ldd, M, N,
-        m_tiles, splits, BN);
+        pl.kbs, grid);
     KVM_CUDA_TRY(cudaGetLastError());
   }
   return KVM_OK;
