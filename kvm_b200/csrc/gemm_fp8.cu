@@ -33,13 +33,14 @@ struct Fp8Params {
   __nv_bfloat16* D;
   long long ldd;
   int* status;
-  // Work split. stream_k: CTA c takes K blocks [c*W/G, (c+1)*W/G) of the
-  // tile-major sequence of all tiles' K blocks (W = tiles * K/128, G =
-  // gridDim.x), so every CTA gets the same number of blocks whatever the
-  // tile count. Only a CTA's first and last segments can be parts of a tile
-  // cut between CTAs; those are written as fp32 partials (slot 2c for the
-  // first, 2c + 1 for the last) and summed by fp8_streamk_reduce_kernel.
-  // Otherwise CTA c takes whole tiles c, c+G, ...
+  // Work split. Whole tiles round-robin (CTA c: tiles c, c+G, ...; G =
+  // gridDim.x) for all but the last one to two waves' worth of tiles
+  // (streamk_first_tile); those are split stream-K: CTA c takes K blocks
+  // [c*W/G, (c+1)*W/G) of the tail tiles' K blocks in tile order, so every
+  // CTA ends with the same amount of work. Only a CTA's first and last
+  // stream-K segments can be parts of a tile cut between CTAs; those are
+  // written as fp32 partials (slot 2c for the first, 2c + 1 for the last)
+  // and summed by fp8_streamk_reduce_kernel. stream_k == 0: round-robin only.
   int stream_k;
   float* partial;    // [G][2][128][128] fp32
 };
@@ -67,31 +68,41 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
-// The segments (tile, K blocks [kb0, kb1)) a CTA works through, in order.
+// First tile of the stream-K tail: all tiles when there are fewer than two
+// waves, else all but the last one to two waves (the earlier waves keep the
+// round-robin order, whose concurrent tiles share weight tiles in L2).
+__host__ __device__ __forceinline__ int streamk_first_tile(int tiles, int ctas) {
+  return tiles >= 2 * ctas ? (tiles / ctas - 1) * ctas : 0;
+}
+
+// The segments (tile, K blocks [kb0, kb1)) a CTA works through, in order:
+// round-robin whole tiles below t0, then its stream-K range of the tail.
 struct Fp8Segments {
-  long long x, hi;   // stream-K: next K-block index, end of this CTA's range
-  int t, tiles, step, kbs, stream_k;
+  long long x, hi;   // stream-K: next K-block index of the tail, end of the range
+  int t, t0, tiles, step, kbs;
   __device__ Fp8Segments(const Fp8Params& p, int tiles_, int kbs_)
-      : tiles(tiles_), step(static_cast<int>(gridDim.x)), kbs(kbs_), stream_k(p.stream_k) {
-    const long long W = static_cast<long long>(tiles_) * kbs_;
+      : tiles(tiles_), step(static_cast<int>(gridDim.x)), kbs(kbs_) {
+    t0 = p.stream_k ? streamk_first_tile(tiles_, step) : tiles_;
+    const long long W = static_cast<long long>(tiles_ - t0) * kbs_;
     x = W * blockIdx.x / gridDim.x;
     hi = W * (blockIdx.x + 1) / gridDim.x;
     t = static_cast<int>(blockIdx.x);
   }
+  // stream-K segments are the ones with tile >= t0
   __device__ bool next(int& tile, int& kb0, int& kb1) {
-    if (stream_k) {
-      if (x >= hi) return false;
-      tile = static_cast<int>(x / kbs);
-      kb0 = static_cast<int>(x - static_cast<long long>(tile) * kbs);
-      kb1 = static_cast<int>(min(static_cast<long long>(kbs), kb0 + (hi - x)));
-      x += kb1 - kb0;
+    if (t < t0) {
+      tile = t;
+      kb0 = 0;
+      kb1 = kbs;
+      t += step;
       return true;
     }
-    if (t >= tiles) return false;
-    tile = t;
-    kb0 = 0;
-    kb1 = kbs;
-    t += step;
+    if (x >= hi) return false;
+    const int u = static_cast<int>(x / kbs);
+    tile = t0 + u;
+    kb0 = static_cast<int>(x - static_cast<long long>(u) * kbs);
+    kb1 = static_cast<int>(min(static_cast<long long>(kbs), kb0 + (hi - x)));
+    x += kb1 - kb0;
     return true;
   }
 };
@@ -222,7 +233,7 @@ __global__ void __launch_bounds__(f8_threads(EW), 1)
     uint32_t g = 0;
     bool ok = true;
     Fp8Segments seg(p, tiles, kbs);
-    int tile, kb0, kb1, si = 0;
+    int tile, kb0, kb1, si = 0;  // si: stream-K segments so far
     while (ok && seg.next(tile, kb0, kb1)) {
       const int nt = tile / m_tiles, mt = tile - nt * m_tiles;
       float acc[COLS];
@@ -269,7 +280,7 @@ __global__ void __launch_bounds__(f8_threads(EW), 1)
       float* part = whole ? nullptr
                           : p.partial + (static_cast<long long>(blockIdx.x) * 2 + (si ? 1 : 0)) *
                                             (kF8BM * BN);
-      ++si;
+      if (tile >= seg.t0) ++si;
       if (TN) {
         // thread = output column nt*128 + r_in; acc[m] = token m (M <= TN)
         const int col = nt * BN + r_in;
@@ -328,15 +339,18 @@ __global__ void fp8_streamk_reduce_kernel(const float* __restrict__ partial,
   if (i >= static_cast<long long>(M) * N) return;
   const int row = static_cast<int>(i / N), col = static_cast<int>(i % N);
   const int m_tiles = (M + kF8BM - 1) / kF8BM;
-  const long long tile = static_cast<long long>(col / 128) * m_tiles + row / kF8BM;
-  const long long W = static_cast<long long>(m_tiles) * (N / 128) * kbs;
-  const int c_lo = streamk_cta(tile * kbs, W, G);
-  const int c_hi = streamk_cta(tile * kbs + kbs - 1, W, G);
+  const int tiles = m_tiles * (N / 128);
+  const int t0 = streamk_first_tile(tiles, G);
+  const long long u = static_cast<long long>(col / 128) * m_tiles + row / kF8BM - t0;
+  if (u < 0) return;  // a round-robin tile
+  const long long W = static_cast<long long>(tiles - t0) * kbs;
+  const int c_lo = streamk_cta(u * kbs, W, G);
+  const int c_hi = streamk_cta(u * kbs + kbs - 1, W, G);
   if (c_lo == c_hi) return;
   float a[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
   for (int c = c_lo; c <= c_hi; ++c) {
-    const long long first = (W * c / G) / kbs;  // first tile of CTA c
-    const long long slot = static_cast<long long>(c) * 2 + (tile == first ? 0 : 1);
+    const long long first = (W * c / G) / kbs;  // first tail tile of CTA c
+    const long long slot = static_cast<long long>(c) * 2 + (u == first ? 0 : 1);
     const float* src = partial + (slot * kF8BM + row % kF8BM) * 128 + col % 128;
     const float4 x = reinterpret_cast<const float4*>(src)[0];
     const float4 y = reinterpret_cast<const float4*>(src)[1];
@@ -348,9 +362,11 @@ __global__ void fp8_streamk_reduce_kernel(const float* __restrict__ partial,
                  pack_bf16x2(a[4], a[5]), pack_bf16x2(a[6], a[7]));
 }
 
-// Whether stream-K over `ctas` CTAs cuts any of `tiles` tiles of `kbs` K
-// blocks between two CTAs (then partials and a reduction are needed).
-bool streamk_cuts(long long tiles, int kbs, int ctas) {
+// Whether stream-K over `ctas` CTAs cuts any tile of the tail (tiles from
+// streamk_first_tile on) between two CTAs (then partials and a reduction
+// are needed).
+bool streamk_cuts(int tiles_all, int kbs, int ctas) {
+  const long long tiles = tiles_all - streamk_first_tile(tiles_all, ctas);
   const long long W = tiles * kbs;
   for (int c = 1; c < ctas; ++c)
     if ((W * c / ctas) % kbs != 0) return true;

@@ -34,11 +34,12 @@ def test_quantiser_from_bf16(cuda):
 @pytest.mark.parametrize("M,N,K", [(16, 1024, 2048), (128, 512, 1024), (300, 256, 640),
                                    (1024, 1280, 1024), (1, 256, 512), (33, 384, 1024),
                                    (64, 128 * 150, 256), (16, 28672, 1024),
-                                   (200, 128 * 37, 384)])
+                                   (200, 128 * 37, 384), (300, 128 * 100, 256)])
 def test_fp8_gemm(cuda, M, N, K):
     """Every launch form: the swapped form for M <= 64 (16/32/64-token tiles)
     and the 128-row form, each with stream-K tiles cut between CTAs (partials
-    + reduction) or held whole."""
+    + reduction) or held whole, and round-robin waves before a stream-K tail
+    (300 tiles on 148 SMs)."""
     rng = np.random.default_rng(M + N + K)
     a = rng.standard_normal((M, K)).astype(np.float32)
     w = rng.standard_normal((N, K)).astype(np.float32)
