@@ -169,9 +169,13 @@ extern "C" int kvm_sm100_gemm_bf16(const void* A, int64_t lda, const void* B,
   p.D = D; p.ldd = ldd; p.C = C; p.ldc = ldd;
   p.status = dev->status;
 
+  // Output tile width: 256 when those tiles still fill the SMs, 64 when even
+  // 128-wide tiles would leave over half of the SMs idle (small, latency-bound
+  // products: more CTAs each stream fewer bytes), else 128.
   const int m_tiles = cdiv(M, kGemmBM);
   const bool wide = (long long)m_tiles * cdiv(N, 256) >= dev->sm_count;
-  const int BN = wide ? 256 : 128;
+  const bool narrow = !wide && 2LL * m_tiles * cdiv(N, 128) <= dev->sm_count;
+  const int BN = wide ? 256 : narrow ? 64 : 128;
   const int tiles = m_tiles * cdiv(N, BN);
   const int grid = tiles < dev->sm_count ? tiles : dev->sm_count;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
@@ -198,6 +202,12 @@ extern "C" int kvm_sm100_gemm_bf16(const void* A, int64_t lda, const void* B,
     if (!mn && f32) return launch<256, 4, false, kEpiF32>(ta, tb, p, grid, st);
     if (mn && !f32) return launch<256, 4, true, kEpiBf16>(ta, tb, p, grid, st);
     return launch<256, 4, true, kEpiF32>(ta, tb, p, grid, st);
+  }
+  if (narrow) {
+    if (!mn && !f32) return launch<64, 8, false, kEpiBf16>(ta, tb, p, grid, st);
+    if (!mn && f32) return launch<64, 8, false, kEpiF32>(ta, tb, p, grid, st);
+    if (mn && !f32) return launch<64, 8, true, kEpiBf16>(ta, tb, p, grid, st);
+    return launch<64, 8, true, kEpiF32>(ta, tb, p, grid, st);
   }
   if (!mn && !f32) return launch<128, 6, false, kEpiBf16>(ta, tb, p, grid, st);
   if (!mn && f32) return launch<128, 6, false, kEpiF32>(ta, tb, p, grid, st);
