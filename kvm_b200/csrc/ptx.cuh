@@ -76,13 +76,17 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 // another role of the same CTA.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
                                           volatile int* abort) {
-  if (mbar_try_wait(bar, parity)) return true;
-  const uint64_t t0 = globaltimer_ns();
-  for (uint32_t i = 1;; ++i) {
+  // The clock starts after 64 unsuccessful polls (each try_wait itself blocks
+  // for a bounded time), so a wait that ends soon never reads the timer.
+  uint64_t t0 = 0;
+  for (uint32_t i = 0;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
-    if ((i & 63u) == 0) {
+    if ((i & 63u) == 63u) {
       if (*abort) return false;
-      if (globaltimer_ns() - t0 > kWaitTimeoutNs) {
+      const uint64_t now = globaltimer_ns();
+      if (t0 == 0) {
+        t0 = now;
+      } else if (now - t0 > kWaitTimeoutNs) {
         *abort = 1;
         return false;
       }
@@ -369,13 +373,15 @@ __device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar,
 // Bounded wait for a phase completed by arrivals from either CTA.
 __device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity,
                                                   volatile int* abort) {
-  if (mbar_try_wait_cluster(bar, parity)) return true;
-  const uint64_t t0 = globaltimer_ns();
-  for (uint32_t i = 1;; ++i) {
+  uint64_t t0 = 0;  // as mbar_wait: the clock starts after 64 polls
+  for (uint32_t i = 0;; ++i) {
     if (mbar_try_wait_cluster(bar, parity)) return true;
-    if ((i & 63u) == 0) {
+    if ((i & 63u) == 63u) {
       if (*abort) return false;
-      if (globaltimer_ns() - t0 > kWaitTimeoutNs) {
+      const uint64_t now = globaltimer_ns();
+      if (t0 == 0) {
+        t0 = now;
+      } else if (now - t0 > kWaitTimeoutNs) {
         *abort = 1;
         return false;
       }
