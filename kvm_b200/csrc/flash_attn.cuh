@@ -258,7 +258,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           tmem_ld32(tmem_base + lane_off + b * 128 + c4 * 32, u);
           tmem_wait_ld();
 #pragma unroll
-          for (int i = 0; i < 32; ++i) s[c4 * 32 + i] = __uint_as_float(u[i]) * sl2;
+          for (int i = 0; i < 32; ++i) s[c4 * 32 + i] = __fmul_rn(__uint_as_float(u[i]), sl2);
         }
         tc_fence_before();
         mbar_arrive(&s_free[b]);
