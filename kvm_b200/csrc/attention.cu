@@ -3,10 +3,9 @@
 // (src/ir/dialect/kernel/dialect.cpp:38-40) for the tensor-parallel decoder
 // layer.
 //
-// Attention runs as one fused kernel: S and O in TMEM, online softmax in
-// registers, P through shared memory; scores never reach HBM. Two query
-// heads per CTA in ping-pong (flash_attn_pp.cuh) when the group size is
-// even, else one query tile per CTA (flash_attn.cuh). (An earlier form ran S = QK^T, a softmax pass and PV as three
+// Attention runs as one fused kernel (flash_attn.cuh): S and O in TMEM,
+// online softmax in registers, P through shared memory; scores never reach
+// HBM. (An earlier form ran S = QK^T, a softmax pass and PV as three
 // launches through an L x L fp32 workspace: 3.7 ms and 74 TF/s on the
 // decoder layer's attention, against 0.45 ms and 609 TF/s fused.)
 // Grouped-query heads map q head h to kv head h / (HQ / HKV).
@@ -14,10 +13,7 @@
 
 #include <cmath>
 
-#include <cstdlib>
-
 #include "flash_attn.cuh"
-#include "flash_attn_pp.cuh"
 #include "gemm_bf16.cuh"
 #include "runtime.h"
 
@@ -106,19 +102,6 @@ extern "C" int kvm_sm100_attention_prefill_bf16(
   const long long items = static_cast<long long>(B) * HQ * ap.q_tiles;
   if (items > (1ll << 30))
     return fail(KVM_ERR_INVALID_ARG, "attention: too many (batch, head, tile) items");
-  // Two query heads per CTA in ping-pong when a kv head serves an even number
-  // of query heads (KVM_SM100_ATTN_PINGPONG=0 selects the one-tile kernel).
-  const char* pp_env = std::getenv("KVM_SM100_ATTN_PINGPONG");
-  if (group % 2 == 0 && !(pp_env && pp_env[0] == '0')) {
-    const long long pairs = items / 2;
-    const int grid = pairs < dev->sm_count ? int(pairs) : dev->sm_count;
-    constexpr size_t smem = attn_pp_smem_bytes();
-    KVM_CUDA_TRY(cudaFuncSetAttribute(attn_fwd_pp_kernel,
-                                      cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
-    attn_fwd_pp_kernel<<<grid, kPpThreads, smem, st>>>(tq, tk, tv, ap);
-    KVM_CUDA_TRY(cudaGetLastError());
-    return KVM_OK;
-  }
   const int grid = items < dev->sm_count ? int(items) : dev->sm_count;
   constexpr size_t smem = attn_smem_bytes();
   KVM_CUDA_TRY(cudaFuncSetAttribute(attn_fwd_kernel,

@@ -82,28 +82,3 @@ def test_attention_rescales_when_later_keys_dominate(cuda):
     assert np.isfinite(got).all()
     assert rel_err(got, oracle.bf16_to_f32(ref)) < 1e-2
 
-
-@pytest.mark.parametrize("B,L,HQ,HKV", [(2, 512, 8, 2), (1, 1000, 4, 1), (3, 136, 2, 1),
-                                        (1, 2048, 16, 2)])
-def test_pingpong_kernel_equals_one_tile_kernel(cuda, B, L, HQ, HKV):
-    """The two-heads-per-CTA ping-pong kernel (even group sizes) computes
-    exactly what the one-tile kernel computes: same MMA orders, same online
-    softmax arithmetic."""
-    import os
-    rng = np.random.default_rng(B * 7 + L + HQ)
-    hd = 128
-    q = from_bits(oracle.normal_bf16(rng, (B * L, HQ * hd)), cuda)
-    k = from_bits(oracle.normal_bf16(rng, (B * L, HKV * hd)), cuda)
-    v = from_bits(oracle.normal_bf16(rng, (B * L, HKV * hd)), cuda)
-    pp = ops.attention_prefill(q, k, v, batch=B, heads_q=HQ, heads_kv=HKV)
-    ops.device_status()
-    os.environ["KVM_SM100_ATTN_PINGPONG"] = "0"
-    try:
-        one = ops.attention_prefill(q, k, v, batch=B, heads_q=HQ, heads_kv=HKV)
-        ops.device_status()
-    finally:
-        del os.environ["KVM_SM100_ATTN_PINGPONG"]
-    assert torch.equal(pp.view(torch.int16), one.view(torch.int16))
-    if L <= 1000:
-        ref = oracle.attention(to_bits(q), to_bits(k), to_bits(v), B, HQ, HKV)
-        assert rel_err(oracle.bf16_to_f32(to_bits(pp)), oracle.bf16_to_f32(ref)) < 1e-2
