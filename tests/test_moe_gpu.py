@@ -129,6 +129,36 @@ def test_grouped_gemm_wide_groups(cuda, silu):
             assert rel_err(g[lo:hi], r[lo:hi]) < 1e-2, i
 
 
+@pytest.mark.parametrize("silu", [False, True])
+def test_grouped_gemm_groups_just_past_one_tile(cuda, silu):
+    """Groups of 257..289 tokens (two token tiles of 136..152 columns) beside
+    groups of every other size class, each group checked on its own rows, and
+    nothing written past the last row."""
+    rng = np.random.default_rng(29 + silu)
+    K = 256
+    N = 512 if silu else 768
+    counts = np.array([257, 264, 270, 272, 273, 280, 287, 288, 289, 256, 255, 1, 0, 300,
+                       258, 520])
+    G = len(counts)
+    off = np.concatenate([[0], np.cumsum(counts)]).astype(np.int32)
+    rows = int(off[-1])
+    a = oracle.normal_bf16(rng, (rows, K))
+    w = oracle.normal_bf16(rng, (G, N, K), 0.05)
+    ref = oracle.grouped_gemm(a, w, off, silu_gate=silu)
+    out_n = N // 2 if silu else N
+    canary = torch.full((rows + 64, out_n), 7.0, dtype=torch.bfloat16, device=cuda)
+    got = ops.grouped_matmul(from_bits(a, cuda), from_bits(w, cuda),
+                             torch.from_numpy(off).to(cuda), silu_gate=silu,
+                             out=canary[:rows])
+    ops.device_status()
+    assert torch.all(canary[rows:] == 7.0)  # nothing written past the last row
+    g, r = oracle.bf16_to_f32(to_bits(got)), oracle.bf16_to_f32(ref)
+    for i in range(G):
+        lo, hi = off[i], off[i + 1]
+        if hi > lo:
+            assert rel_err(g[lo:hi], r[lo:hi]) < 1e-2, (i, counts[i])
+
+
 def test_combine_bit_exact(cuda):
     rng = np.random.default_rng(31)
     T, k, H, E = 777, 2, 512, 64
