@@ -107,27 +107,46 @@ __global__ void __launch_bounds__(kPermChunk)
   }
 }
 
-// One block per token: read its row once, write it to each of its k rows.
-__global__ void __launch_bounds__(256)
+// Rows of TOK tokens per block: every thread first loads all its 16-byte
+// vectors of the TOK rows (TOK x VPT loads in flight per thread, enough to
+// cover HBM latency at full occupancy), then writes each to the token's k
+// destination rows. VPT = vectors per thread per row (row_vecs <= 256 VPT).
+constexpr int kScatterTok = 4;
+constexpr int kRowThreads = 256;
+
+template <int VPT>
+__global__ void __launch_bounds__(kRowThreads)
     scatter_rows_kernel(const uint4* __restrict__ x, const int* __restrict__ pos,
-                        uint4* __restrict__ xp, int k, int row_vecs,
+                        uint4* __restrict__ xp, int T, int k, int row_vecs,
                         long long n_rows_out, int* status) {
-  const int t = blockIdx.x;
-  int dst[8];
+  const int t0 = blockIdx.x * kScatterTok;
+  uint4 val[kScatterTok][VPT];
 #pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    dst[j] = j < k ? pos[static_cast<long long>(t) * k + j] : -1;
-    if (j < k && (dst[j] < 0 || dst[j] >= n_rows_out)) {
-      if (threadIdx.x == 0) atomicOr(status, kDevBadInput);
-      dst[j] = -1;
+  for (int i = 0; i < kScatterTok; ++i) {
+    const int t = t0 + i;
+#pragma unroll
+    for (int c = 0; c < VPT; ++c) {
+      const int v = threadIdx.x + c * kRowThreads;
+      if (t < T && v < row_vecs) val[i][c] = __ldg(x + static_cast<long long>(t) * row_vecs + v);
     }
   }
-  const uint4* src = x + static_cast<long long>(t) * row_vecs;
-  for (int v = threadIdx.x; v < row_vecs; v += blockDim.x) {
-    const uint4 val = __ldg(src + v);
 #pragma unroll
-    for (int j = 0; j < 8; ++j)
-      if (dst[j] >= 0) xp[static_cast<long long>(dst[j]) * row_vecs + v] = val;
+  for (int i = 0; i < kScatterTok; ++i) {
+    const int t = t0 + i;
+    if (t >= T) break;
+    for (int j = 0; j < k; ++j) {
+      int d = pos[static_cast<long long>(t) * k + j];
+      if (d < 0 || d >= n_rows_out) {
+        if (threadIdx.x == 0) atomicOr(status, kDevBadInput);
+        continue;
+      }
+      uint4* dst = xp + static_cast<long long>(d) * row_vecs;
+#pragma unroll
+      for (int c = 0; c < VPT; ++c) {
+        const int v = threadIdx.x + c * kRowThreads;
+        if (v < row_vecs) dst[v] = val[i][c];
+      }
+    }
   }
 }
 
@@ -145,37 +164,70 @@ __device__ __forceinline__ uint32_t pack2(float a, float b) {
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
-// One block per token: out[t] = sum_j w[t,j] * Y[pos[t,j]] in fp32, j in order,
-// each step one fused multiply-add (a = fma(w, y, a)) starting from a = 0.
-__global__ void __launch_bounds__(256)
+// TOK tokens per block: out[t] = sum_j w[t,j] * Y[pos[t,j]] in fp32, j in
+// order, each step one fused multiply-add (a = fma(w, y, a)) starting from
+// a = 0. Every thread loads its vectors of the first KL sources of its TOK
+// tokens before the arithmetic (further sources, k > KL, load as they go).
+constexpr int kCombineTok = 1;
+constexpr int kCombineKL = 2;
+
+template <int VPT>
+__global__ void __launch_bounds__(kRowThreads)
     combine_kernel(const uint4* __restrict__ Y, const int* __restrict__ pos,
-                   const float* __restrict__ w, uint4* __restrict__ out, int k,
+                   const float* __restrict__ w, uint4* __restrict__ out, int T, int k,
                    int row_vecs, long long n_rows_y, int* status) {
-  const int t = blockIdx.x;
-  int src[8];
-  float wt[8];
+  const int t0 = blockIdx.x * kCombineTok;
+  int src[kCombineTok][8];
+  float wt[kCombineTok][8];
 #pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    src[j] = j < k ? pos[static_cast<long long>(t) * k + j] : -1;
-    wt[j] = j < k ? w[static_cast<long long>(t) * k + j] : 0.f;
-    if (j < k && (src[j] < 0 || src[j] >= n_rows_y)) {
-      if (threadIdx.x == 0) atomicOr(status, kDevBadInput);
-      src[j] = -1;
+  for (int i = 0; i < kCombineTok; ++i) {
+    const int t = t0 + i;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const bool on = t < T && j < k;
+      src[i][j] = on ? pos[static_cast<long long>(t) * k + j] : -1;
+      wt[i][j] = on ? w[static_cast<long long>(t) * k + j] : 0.f;
+      if (on && (src[i][j] < 0 || src[i][j] >= n_rows_y)) {
+        if (threadIdx.x == 0) atomicOr(status, kDevBadInput);
+        src[i][j] = -1;
+      }
     }
   }
-  for (int v = threadIdx.x; v < row_vecs; v += blockDim.x) {
-    float a[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  uint4 y[kCombineTok][kCombineKL][VPT];
 #pragma unroll
-    for (int j = 0; j < 8; ++j)
-      if (src[j] >= 0)
-        acc_bf16x8(a, __ldg(Y + static_cast<long long>(src[j]) * row_vecs + v),
-                   wt[j]);
-    uint4 o;
-    o.x = pack2(a[0], a[1]);
-    o.y = pack2(a[2], a[3]);
-    o.z = pack2(a[4], a[5]);
-    o.w = pack2(a[6], a[7]);
-    out[static_cast<long long>(t) * row_vecs + v] = o;
+  for (int i = 0; i < kCombineTok; ++i)
+#pragma unroll
+    for (int j = 0; j < kCombineKL; ++j)
+#pragma unroll
+      for (int c = 0; c < VPT; ++c) {
+        const int v = threadIdx.x + c * kRowThreads;
+        if (src[i][j] >= 0 && v < row_vecs)
+          y[i][j][c] = __ldg(Y + static_cast<long long>(src[i][j]) * row_vecs + v);
+      }
+#pragma unroll
+  for (int i = 0; i < kCombineTok; ++i) {
+    const int t = t0 + i;
+    if (t >= T) break;
+#pragma unroll
+    for (int c = 0; c < VPT; ++c) {
+      const int v = threadIdx.x + c * kRowThreads;
+      if (v >= row_vecs) continue;
+      float a[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        if (src[i][j] < 0) continue;
+        const uint4 yv = j < kCombineKL
+                             ? y[i][j < kCombineKL ? j : 0][c]
+                             : __ldg(Y + static_cast<long long>(src[i][j]) * row_vecs + v);
+        acc_bf16x8(a, yv, wt[i][j]);
+      }
+      uint4 o;
+      o.x = pack2(a[0], a[1]);
+      o.y = pack2(a[2], a[3]);
+      o.z = pack2(a[4], a[5]);
+      o.w = pack2(a[6], a[7]);
+      out[static_cast<long long>(t) * row_vecs + v] = o;
+    }
   }
 }
 
@@ -242,9 +294,20 @@ extern "C" int kvm_sm100_moe_scatter_rows(const void* x, const int32_t* pos,
                 "moe_scatter_rows: NULL or unaligned pointer");
   const DeviceInfo* dev = device_info();
   if (!dev) return KVM_ERR_CUDA;
-  scatter_rows_kernel<<<T, 256, 0, static_cast<cudaStream_t>(stream)>>>(
-      static_cast<const uint4*>(x), pos, static_cast<uint4*>(xp), k, H / 8,
-      static_cast<long long>(T) * k, dev->status);
+  const int row_vecs = H / 8;
+  const unsigned blocks = static_cast<unsigned>((T + kScatterTok - 1) / kScatterTok);
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const long long n_out = static_cast<long long>(T) * k;
+  const uint4* xv = static_cast<const uint4*>(x);
+  uint4* xpv = static_cast<uint4*>(xp);
+  if (row_vecs <= kRowThreads)
+    scatter_rows_kernel<1><<<blocks, kRowThreads, 0, st>>>(xv, pos, xpv, T, k, row_vecs, n_out, dev->status);
+  else if (row_vecs <= 2 * kRowThreads)
+    scatter_rows_kernel<2><<<blocks, kRowThreads, 0, st>>>(xv, pos, xpv, T, k, row_vecs, n_out, dev->status);
+  else if (row_vecs <= 4 * kRowThreads)
+    scatter_rows_kernel<4><<<blocks, kRowThreads, 0, st>>>(xv, pos, xpv, T, k, row_vecs, n_out, dev->status);
+  else
+    return fail(KVM_ERR_UNSUPPORTED, "moe_scatter_rows: rows wider than 8192 elements");
   KVM_CUDA_TRY(cudaGetLastError());
   return KVM_OK;
 }
@@ -259,9 +322,20 @@ extern "C" int kvm_sm100_moe_combine(const void* Y, const int32_t* pos,
     return fail(KVM_ERR_INVALID_ARG, "moe_combine: NULL or unaligned pointer");
   const DeviceInfo* dev = device_info();
   if (!dev) return KVM_ERR_CUDA;
-  combine_kernel<<<T, 256, 0, static_cast<cudaStream_t>(stream)>>>(
-      static_cast<const uint4*>(Y), pos, w, static_cast<uint4*>(out), k, H / 8,
-      static_cast<long long>(T) * k, dev->status);
+  const int row_vecs = H / 8;
+  const unsigned blocks = static_cast<unsigned>((T + kCombineTok - 1) / kCombineTok);
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const long long n_y = static_cast<long long>(T) * k;
+  const uint4* yv = static_cast<const uint4*>(Y);
+  uint4* ov = static_cast<uint4*>(out);
+  if (row_vecs <= kRowThreads)
+    combine_kernel<1><<<blocks, kRowThreads, 0, st>>>(yv, pos, w, ov, T, k, row_vecs, n_y, dev->status);
+  else if (row_vecs <= 2 * kRowThreads)
+    combine_kernel<2><<<blocks, kRowThreads, 0, st>>>(yv, pos, w, ov, T, k, row_vecs, n_y, dev->status);
+  else if (row_vecs <= 4 * kRowThreads)
+    combine_kernel<4><<<blocks, kRowThreads, 0, st>>>(yv, pos, w, ov, T, k, row_vecs, n_y, dev->status);
+  else
+    return fail(KVM_ERR_UNSUPPORTED, "moe_combine: rows wider than 8192 elements");
   KVM_CUDA_TRY(cudaGetLastError());
   return KVM_OK;
 }
