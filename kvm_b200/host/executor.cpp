@@ -771,6 +771,19 @@ void Executor::PlanComm(const ir::OpNode* op) {
   }
   const ir::OpNode* kop = KernelCommOp(name, nth);
   const ir::ValueNode* res = op->results()[0];
+  if (name == "comm.moe_dispatch" || name == "comm.moe_combine") {
+    // Expert parallelism across ranks (tokens exchanged between the experts'
+    // owners) is the Python layer kvm_b200.ep; a graph op over one rank runs
+    // here. Anything else fails rather than silently computing one rank's part.
+    std::vector<int> ranks;
+    if (const auto* r = op->op().impl.as<ir::kernel::MoeDispatch>()) ranks = r->ranks;
+    if (const auto* r = op->op().impl.as<ir::kernel::MoeCombine>()) ranks = r->ranks;
+    std::sort(ranks.begin(), ranks.end());
+    ranks.erase(std::unique(ranks.begin(), ranks.end()), ranks.end());
+    if (ranks.size() > 1)
+      Fail("'" + name + "' over " + std::to_string(ranks.size()) +
+           " ranks: expert parallelism runs through kvm_b200.ep, not the graph executor");
+  }
   if (name == "comm.moe_dispatch") {
     const Buffer x = GlobalOf(op->operands()[0]);
     const Buffer g = GlobalOf(op->operands()[1]);

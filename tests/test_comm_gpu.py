@@ -133,3 +133,23 @@ def test_collectives_over_nccl(cuda, tmp_path, world):
                 np.testing.assert_allclose(got, ref, rtol=1e-5, atol=1e-5)
                 continue
             assert np.array_equal(got, np.asarray(w).reshape(-1)), (rk, k)
+
+
+@pytest.mark.gpu
+def test_expert_parallel_graph_ops_fail_loudly(cuda, tmp_path):
+    """moe_dispatch over more than one rank is expert parallelism, which runs
+    through kvm_b200.ep; the graph executor refuses it instead of computing
+    one rank's share."""
+    if not KVM_RUN.exists():
+        pytest.fail("kvm_run is not built")
+    T, H, E = 64, 128, 8
+    g = tmp_path / "ep.kvm"
+    g.write_text(f"""graph {{
+  config {{ ranks = [0, 1] }}
+  ^ep(%x: {_t('bf16', [T, H])}, %g: {_t('f32', [T, E])}) {{
+    %d: {_t('bf16', [2 * T, H])} = kernel.comm.moe_dispatch<ranks=[0,1]> {{top_k = 2}} (%x, %g)
+    return %d
+  }}
+}}""")
+    r = subprocess.run([str(KVM_RUN), str(g)], capture_output=True, text=True, timeout=120)
+    assert r.returncode == 1 and "expert parallelism" in r.stderr, r.stderr
