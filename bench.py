@@ -192,6 +192,30 @@ def cpu_baseline_leg(x_dev, wr, w13, w2, min_s: float = 10.0) -> dict:
                       f"(same inputs and weights), {dt:.1f} s"}
 
 
+def cpu_job(name, args, kw, units, unit, sample, max_reps, min_s=3.0):
+    """CPU baseline of a kernel workload line: the oracle's `name` on the host
+    cores over a bounded sample, repeated until min_s of work (at most
+    max_reps); `units` of the line's unit per call."""
+    import oracle
+    if name == "mlp_rows":
+        x, wg, wu, wd = args
+        fn = lambda: oracle.gemm(oracle.gemm_silu_gate(oracle.rmsnorm(x, None, 1e-5), wg, wu),
+                                 wd, b_layout="nk")
+    else:
+        f = getattr(oracle, name)
+        fn = lambda: f(*args, **kw)
+    fn()  # warm-up
+    done, t0 = 0, time.perf_counter()
+    while True:
+        fn()
+        done += 1
+        dt = time.perf_counter() - t0
+        if dt >= min_s or done >= max_reps:
+            break
+    return {"value": units * done / dt, "unit": unit, "cores": oracle.num_threads(),
+            "kind": "port", "sample": f"{sample}, x{done} in {dt:.1f} s"}
+
+
 def run_ours(args) -> int:
     import torch
     import torch.distributed as dist
@@ -413,6 +437,8 @@ def main(argv=None) -> int:
     args = parse_args(argv)
     if args.workload != "moe":
         from kvm_b200 import bench_kernels
+        if not args.no_cpu_baseline and int(os.environ.get("RANK", "0")) == 0:
+            bench_kernels.CPU_LEG = cpu_job
         return bench_kernels.run(args, peaks(), ClockSampler)
     if args.impl == "reference":
         return run_reference(args)

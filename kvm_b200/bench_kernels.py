@@ -58,6 +58,24 @@ def _time(fn, steps, warmup, flush=None):
     return statistics.mean(a.elapsed_time(b) for a, b in ts)
 
 
+# Set by bench.py: runs a CPU-baseline job (the oracle on the host cores) and
+# returns its cpu_baseline dict. This package never touches the oracle itself.
+CPU_LEG = None
+
+
+def _cpu_job(name, args, units, unit, sample, max_reps=20, **kw):
+    """The CPU baseline of a line: job `name` on `args` processes `units` of the
+    metric's unit per call; None when no CPU leg is wired in."""
+    if CPU_LEG is None:
+        return None
+    return CPU_LEG(name, args, kw, units, unit, sample, max_reps)
+
+
+def _bits(t):
+    import numpy as np
+    return t.contiguous().view(torch.int16).cpu().numpy().view(np.uint16)
+
+
 def _l2_flusher(dev):
     """Evict L2 (126 MB) by reading 256 MB: the lines left behind are clean,
     so the timed kernel's misses do not also pay for write-backs of a flush."""
@@ -183,8 +201,14 @@ def run_attn(args, peaks, ClockSampler, dev, g) -> int:
     # causal: keys 0..pos for each query -> 2 * (L (L + 1) / 2) * 128 * 2 per head
     flop = 4.0 * B * HQ * 128 * (L * (L + 1) / 2)
     tf = flop / (ms / 1e3) / 1e12
+    grp = HQ // HKV
+    cpu = _cpu_job("attention", (_bits(q[:, :grp * 128]), _bits(k[:, :128]), _bits(v[:, :128]),
+                                 B, grp, 1),
+                   flop * grp / HQ / 1e12, "TFLOP/s",
+                   f"the {grp} query heads of kv head 0 (of {HQ}), all {B} x {L} rows",
+                   max_reps=3)
     _line(args, ck, t0, t1, metric="causal attention TFLOP/s", value=tf, unit="TFLOP/s",
-          ms_per_step=ms, dtype="bf16",
+          ms_per_step=ms, dtype="bf16", cpu_baseline=cpu,
           config={"workload": f"causal_gqa_attention_B{B}_L{L}_HQ{HQ}_HKV{HKV}_hd128",
                   "l2": "168 MB of q/k/v > L2"},
           roofline={"bound": "tensor", "achieved": tf, "peak": peaks["bf16"],
@@ -228,8 +252,16 @@ def run_decode(args, peaks, ClockSampler, dev, g) -> int:
     byt = kv_bytes + 2 * S * HQ * 128 * 2 + 2 * S * HKV * 128 * 2
     gbs = byt / (ms / 1e3) / 1e9
     flop = 4.0 * S * HQ * keys * 128
+    n_cpu = min(S, 8)
+    cpu = _cpu_job("attention_decode",
+                   (_bits(q[:n_cpu]), _bits(cache.pool), cache.strides, bs, 0,
+                    q_off[:n_cpu + 1].cpu().numpy(), q_pos[:n_cpu].cpu().numpy(),
+                    perm.cpu().numpy(), bt_off[:n_cpu + 1].cpu().numpy(), HQ, HKV),
+                   byt * n_cpu / S / 1e9, "GB/s",
+                   f"decode attention of {n_cpu} of the {S} sequences (K/V already written)",
+                   max_reps=5)
     _line(args, ck, t0, t1, metric="paged decode attention GB/s", value=gbs, unit="GB/s",
-          ms_per_step=ms, dtype="bf16",
+          ms_per_step=ms, dtype="bf16", cpu_baseline=cpu,
           config={"workload": f"paged_decode_S{S}_ctx4096_HQ64_HKV8_hd128_bs16",
                   "kv_bytes_per_step": kv_bytes, "tflops": flop / (ms / 1e3) / 1e12,
                   "l2": f"{kv_bytes / 1e9:.2f} GB of K/V per step > L2"},
@@ -279,8 +311,16 @@ def run_ew(args, peaks, ClockSampler, dev, g) -> int:
     byt = 3 * 2 * T * F
     gbs = byt / (ms / 1e3) / 1e9
     norm_bytes = 2 * 2 * T * H + 4 * T + 2 * H
+    n_cpu = 1 << 22
+    cpu = _cpu_job("elementwise",
+                   (SILU_PROGRAM, [(_bits(gt.view(-1)[:n_cpu]), "bf16"),
+                                   (_bits(ut.view(-1)[:n_cpu]), "bf16"),
+                                   (one.view(1).cpu().numpy(), "f32")],
+                    [(n_cpu, 1), (n_cpu, 1), (1, 1)], "bf16", 7, n_cpu),
+                   6.0 * n_cpu / 1e9, "GB/s",
+                   f"the program over {n_cpu} of the {T * F} elements", max_reps=5)
     _line(args, ck, t0, t1, metric="fused elementwise GB/s", value=gbs, unit="GB/s",
-          ms_per_step=ms, dtype="f32 registers, bf16 in/out",
+          ms_per_step=ms, dtype="f32 registers, bf16 in/out", cpu_baseline=cpu,
           config={"workload": f"silu_gate_program_{T}x{F}_bf16",
                   "bytes_per_step": byt, "l2": f"{byt / 1e9:.2f} GB per step > L2",
                   "interpreter_ms": ms_i,
@@ -313,8 +353,10 @@ def run(args, peaks, ClockSampler) -> int:
             t1 = time.time()
         flop = 2.0 * 1024 ** 3
         tf = flop / (ms / 1e3) / 1e12
+        cpu = _cpu_job("gemm", (_bits(a), _bits(b)), flop / 1e12, "TFLOP/s",
+                       "the whole 1024^3 product")
         _line(args, ck, t0, t1, metric="GEMM TFLOP/s", value=tf, unit="TFLOP/s",
-              ms_per_step=ms, dtype="bf16",
+              ms_per_step=ms, dtype="bf16", cpu_baseline=cpu,
               config={"workload": "bf16_matmul_1024x1024x1024",
                       "l2": "flushed before each launch (256 MB read)"},
               roofline={"bound": "tensor", "achieved": tf, "peak": peaks["bf16"],
@@ -334,7 +376,7 @@ def run(args, peaks, ClockSampler) -> int:
         wu = (torch.randn((F, H), generator=g, device=dev) * 0.02).to(torch.bfloat16)
         wd = (torch.randn((H, F), generator=g, device=dev) * 0.02).to(torch.bfloat16)
         w13 = ops.pack_gate_up(wg, wu, layout="nk")
-        del wg, wu
+        wg_keep, wu_keep = wg, wu  # for the CPU leg
         xn = torch.empty_like(x)
         h = torch.empty((T, F), dtype=torch.bfloat16, device=dev)
         y = torch.empty((T, H), dtype=torch.bfloat16, device=dev)
@@ -351,8 +393,13 @@ def run(args, peaks, ClockSampler) -> int:
         flop = 2.0 * T * H * F * 3
         tf = flop / (ms / 1e3) / 1e12
         gu_tf = 2.0 * T * H * 2 * F / (t_gu / 1e3) / 1e12
+        rows = 128
+        cpu = _cpu_job("mlp_rows", (_bits(x[:rows]), _bits(wg_keep), _bits(wu_keep), _bits(wd)),
+                       2.0 * rows * H * F * 3 / 1e12, "TFLOP/s",
+                       f"{rows} of the {T} token rows through the block (rows are independent)")
         _line(args, ck, t0, t1, metric="gated MLP block TFLOP/s", value=tf, unit="TFLOP/s",
               ms_per_step=ms, dtype="bf16",
+              cpu_baseline=cpu,
               config={"workload": "gated_mlp_T4096_H4096_F14336", "l2": "weights 352 MB > L2"},
               roofline={"bound": "tensor", "achieved": gu_tf, "peak": peaks["bf16_sustained"],
                         "unit": "TFLOP/s", "frac": gu_tf / peaks["bf16_sustained"],
@@ -388,8 +435,14 @@ def run(args, peaks, ClockSampler) -> int:
     rows = {str(M): dict(r, frac_hbm=r["gbs"] / peaks["hbm"],
                          frac_fp8=r["tflops"] / fp8_peak) for M, r in res.items()}
     r16 = res[16]
+    a16 = torch.randn((16, K), generator=g, device=dev)
+    aq16, sa16 = ops.quantize_e4m3(a16)
+    cpu = _cpu_job("gemm_fp8_blockscaled", (aq16.cpu().numpy(), sa16.cpu().numpy(),
+                                            wq.cpu().numpy(), sw.cpu().numpy()),
+                   r16["bytes"] / 1e9, "GB/s", "the whole M = 16 product", max_reps=5)
     _line(args, ck, t0, t1, metric="FP8 W8A8 GEMM GB/s (M=16, HBM-bound)",
           value=r16["gbs"], unit="GB/s", ms_per_step=r16["ms"], dtype="e4m3",
+          cpu_baseline=cpu,
           config={"workload": "fp8_w8a8_blockscaled_K8192_N28672", "per_m": rows,
                   "fp8_peak_tflops": f"{fp8_peak:.0f} (2 x measured bf16)"},
           roofline={"bound": "hbm", "achieved": r16["gbs"], "peak": peaks["hbm"],
