@@ -462,6 +462,7 @@ namespace {
 struct Fp8Plan {
   int tn;         // 0, or the swapped form's token tile (16, 32, 64)
   int tiles, kbs, ctas;
+  bool use_sk;        // stream-K at all (else whole tiles round-robin)
   bool cuts;          // stream-K cuts tiles: partials + reduction
   int64_t workspace;  // bytes of fp32 partials stream-K needs (0: none)
 };
@@ -473,7 +474,12 @@ Fp8Plan fp8_plan(int M, int N, int K, int sms) {
   pl.kbs = K / kF8BK;
   const long long W = static_cast<long long>(pl.tiles) * pl.kbs;
   pl.ctas = static_cast<int>(W < sms ? W : sms);
-  pl.cuts = streamk_cuts(pl.tiles, pl.kbs, pl.ctas);
+  // The swapped form always balances its K blocks stream-K (its CTAs stream
+  // weights at a rate set by their bytes in flight, so equal shares pay);
+  // the 128-row form only when its tiles do not fill the SMs: measured at
+  // M = 128 (224 tiles), round-robin 64.4 us against 66.2 us stream-K.
+  pl.use_sk = pl.tn != 0 || pl.tiles < pl.ctas;
+  pl.cuts = pl.use_sk && streamk_cuts(pl.tiles, pl.kbs, pl.ctas);
   pl.workspace = pl.cuts ? static_cast<int64_t>(pl.ctas) * 2 * kF8BM * 128 * 4 : 0;
   return pl;
 }
@@ -520,8 +526,8 @@ extern "C" int kvm_sm100_gemm_fp8_blockscaled(const void* Aq, const float* sA,
   const Fp8Plan pl = fp8_plan(M, N, K, dev->sm_count);
   // Stream-K needs room for the partials; without it each CTA takes whole
   // tiles in turn.
-  const bool stream_k = !pl.cuts ||
-                        (workspace && workspace_bytes >= pl.workspace && aligned16(workspace));
+  const bool stream_k = pl.use_sk && (!pl.cuts || (workspace && workspace_bytes >= pl.workspace &&
+                                                    aligned16(workspace)));
   Fp8Params p{M, N, K, sA, sW, static_cast<__nv_bfloat16*>(D), ldd, dev->status,
               stream_k ? 1 : 0, static_cast<float*>(workspace)};
   const int grid = stream_k ? pl.ctas : (pl.tiles < dev->sm_count ? pl.tiles : dev->sm_count);
