@@ -72,3 +72,19 @@ def test_kernels_built_for_sm100a_only():
         pytest.skip("cuobjdump unavailable")
     archs = {line.split(".")[-2] for line in out.stdout.split() if line.endswith(".cubin")}
     assert archs == {"sm_100a"}, archs
+
+
+def test_fp8_workspace_plan():
+    """The FP8 GEMM's workspace query (host-side plan, no GPU needed, 148 SMs
+    assumed without a device): the swapped form (M <= 64) splits K blocks
+    stream-K and needs two fp32 partial tiles per CTA when tiles are cut; the
+    128-row form with tiles enough for every SM takes whole tiles and needs
+    none; tiles fewer than SMs are split (partials again)."""
+    L = _lib.lib()
+    part = 2 * 128 * 128 * 4
+    assert L.kvm_sm100_gemm_fp8_workspace(16, 28672, 8192) == 148 * part
+    assert L.kvm_sm100_gemm_fp8_workspace(128, 28672, 8192) == 0
+    assert L.kvm_sm100_gemm_fp8_workspace(1024, 28672, 8192) == 0
+    assert L.kvm_sm100_gemm_fp8_workspace(128, 1024, 2048) > 0   # 8 tiles on 148 SMs
+    assert L.kvm_sm100_gemm_fp8_workspace(16, 128, 128) == 0      # one block: nothing to cut
+    assert L.kvm_sm100_gemm_fp8_workspace(16, 100, 128) == 0      # N % 128 != 0: invalid
