@@ -76,14 +76,59 @@ __global__ void permute_scan_kernel(const int* __restrict__ counts,
 
 // Rank of each pair among the same-expert pairs before it in its chunk, plus
 // the chunk base: pos[i]; src_token[pos[i]] = i / k.
+//
+// FUSED: `base` is the count matrix instead, and every block derives its own
+// chunk bases and the expert offsets from it (the scans of
+// permute_scan_kernel; block 0 also writes `offsets`), which saves a launch
+// and a single-block pass when the matrix is small (n_chunks * E <= 16 K).
+template <bool FUSED>
 __global__ void __launch_bounds__(kPermChunk)
     permute_rank_kernel(const int* __restrict__ idx, int n, int k, int E,
                         const int* __restrict__ base, int* __restrict__ pos,
-                        int* __restrict__ src_token) {
+                        int* __restrict__ src_token, int n_chunks,
+                        int* __restrict__ offsets) {
   constexpr int kWarps = kPermChunk / 32;
-  extern __shared__ int wcount[];  // [kWarps][E]
+  extern __shared__ int wcount[];  // [kWarps][E], then (FUSED) [2][E]
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   for (int x = threadIdx.x; x < kWarps * E; x += blockDim.x) wcount[x] = 0;
+  int* cbase = wcount + kWarps * E;  // this chunk's base per expert
+  if constexpr (FUSED) {
+    int* tot = cbase + E;
+    for (int e = threadIdx.x; e < E; e += blockDim.x) {
+      int before = 0, all = 0;
+      for (int c = 0; c < n_chunks; ++c) {
+        const int v = base[static_cast<long long>(c) * E + e];
+        before += c < static_cast<int>(blockIdx.x) ? v : 0;
+        all += v;
+      }
+      cbase[e] = before;
+      tot[e] = all;
+    }
+    __syncthreads();
+    // exclusive scan of the expert totals, in place (Hillis-Steele on E <= 1024)
+    for (int d = 1; d < E; d <<= 1) {
+      int add[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int e = threadIdx.x + j * kPermChunk;
+        add[j] = (e < E && e >= d) ? tot[e - d] : 0;
+      }
+      __syncthreads();
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int e = threadIdx.x + j * kPermChunk;
+        if (e < E) tot[e] += add[j];
+      }
+      __syncthreads();
+    }
+    // tot is now inclusive: offsets[e] = tot[e - 1]
+    for (int e = threadIdx.x; e < E; e += blockDim.x) {
+      const int off = e > 0 ? tot[e - 1] : 0;
+      cbase[e] += off;
+      if (blockIdx.x == 0) offsets[e] = off;
+    }
+    if (blockIdx.x == 0 && threadIdx.x == 0) offsets[E] = tot[E - 1];
+  }
   __syncthreads();
   const int i = blockIdx.x * kPermChunk + threadIdx.x;
   int e = -1;
@@ -99,7 +144,7 @@ __global__ void __launch_bounds__(kPermChunk)
   if (e >= 0) {
     int r = rank_in_warp;
     for (int w = 0; w < warp; ++w) r += wcount[w * E + e];
-    const int p = base[static_cast<long long>(blockIdx.x) * E + e] + r;
+    const int p = (FUSED ? cbase[e] : base[static_cast<long long>(blockIdx.x) * E + e]) + r;
     pos[i] = p;
     src_token[p] = i / k;
   } else if (i < n) {
@@ -236,6 +281,42 @@ int n_chunks_of(int T, int k) {
                           kPermChunk);
 }
 
+// The permutation's launches: histogram, then either the scans as their own
+// single-block pass and the ranks, or (small count matrices) the ranks with
+// the scans folded in.
+int launch_permute(const int32_t* topk_idx, int n, int k, int E, int nc, int* counts,
+                   int* base, int32_t* expert_offsets, int32_t* pos, int32_t* src_token,
+                   int* status, cudaStream_t st) {
+  permute_count_kernel<<<nc, kPermChunk, E * sizeof(int), st>>>(topk_idx, n, E, counts,
+                                                                 status);
+  KVM_CUDA_TRY(cudaGetLastError());
+  const size_t rank_smem = (kPermChunk / 32) * E * sizeof(int);
+  if (static_cast<long long>(nc) * E <= 16 * 1024) {
+    const size_t smem = rank_smem + 2 * E * sizeof(int);
+    if (smem > 48 * 1024)
+      KVM_CUDA_TRY(cudaFuncSetAttribute(permute_rank_kernel<true>,
+                                        cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        int(smem)));
+    permute_rank_kernel<true><<<nc, kPermChunk, smem, st>>>(
+        topk_idx, n, k, E, counts, pos, src_token, nc, expert_offsets);
+    KVM_CUDA_TRY(cudaGetLastError());
+    return KVM_OK;
+  }
+  const int scan_threads = ((E + 31) / 32) * 32;
+  permute_scan_kernel<<<1, scan_threads, E * sizeof(int), st>>>(counts, nc, E, base,
+                                                                 expert_offsets);
+  KVM_CUDA_TRY(cudaGetLastError());
+  if (rank_smem > 48 * 1024)
+    KVM_CUDA_TRY(cudaFuncSetAttribute(permute_rank_kernel<false>,
+                                      cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      int(rank_smem)));
+  permute_rank_kernel<false><<<nc, kPermChunk, rank_smem, st>>>(
+      topk_idx, n, k, E, base, pos, src_token, nc, expert_offsets);
+  KVM_CUDA_TRY(cudaGetLastError());
+  return KVM_OK;
+}
+
+
 }  // namespace
 }  // namespace kvm
 
@@ -265,22 +346,8 @@ extern "C" int kvm_sm100_moe_permute(const int32_t* topk_idx, int T, int k,
   const int nc = n_chunks_of(T, k);
   int* counts = static_cast<int*>(workspace);
   int* base = counts + static_cast<long long>(nc) * E;
-  permute_count_kernel<<<nc, kPermChunk, E * sizeof(int), st>>>(
-      topk_idx, n, E, counts, dev->status);
-  KVM_CUDA_TRY(cudaGetLastError());
-  const int scan_threads = ((E + 31) / 32) * 32;
-  permute_scan_kernel<<<1, scan_threads, E * sizeof(int), st>>>(
-      counts, nc, E, base, expert_offsets);
-  KVM_CUDA_TRY(cudaGetLastError());
-  const size_t rank_smem = (kPermChunk / 32) * E * sizeof(int);
-  if (rank_smem > 48 * 1024)
-    KVM_CUDA_TRY(cudaFuncSetAttribute(
-        permute_rank_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-        int(rank_smem)));
-  permute_rank_kernel<<<nc, kPermChunk, rank_smem, st>>>(
-      topk_idx, n, k, E, base, pos, src_token);
-  KVM_CUDA_TRY(cudaGetLastError());
-  return KVM_OK;
+  return launch_permute(topk_idx, n, k, E, nc, counts, base, expert_offsets, pos, src_token,
+                        dev->status, st);
 }
 
 extern "C" int kvm_sm100_moe_scatter_rows(const void* x, const int32_t* pos,
@@ -416,16 +483,6 @@ extern "C" int kvm_sm100_moe_permute_noalloc(const int32_t* topk_idx, int T,
   int* status = scratch + 2 * kNoAllocMaxCells;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const int n = T * k;
-  permute_count_kernel<<<static_cast<int>(nc), kPermChunk, E * sizeof(int), st>>>(
-      topk_idx, n, E, counts, status);
-  KVM_CUDA_TRY(cudaGetLastError());
-  const int scan_threads = ((E + 31) / 32) * 32;
-  permute_scan_kernel<<<1, scan_threads, E * sizeof(int), st>>>(
-      counts, static_cast<int>(nc), E, base, expert_offsets);
-  KVM_CUDA_TRY(cudaGetLastError());
-  const size_t rank_smem = (kPermChunk / 32) * E * sizeof(int);  // <= 32 KiB
-  permute_rank_kernel<<<static_cast<int>(nc), kPermChunk, rank_smem, st>>>(
-      topk_idx, n, k, E, base, pos, src_token);
-  KVM_CUDA_TRY(cudaGetLastError());
-  return KVM_OK;
+  return launch_permute(topk_idx, n, k, E, static_cast<int>(nc), counts, base, expert_offsets,
+                        pos, src_token, status, st);
 }
