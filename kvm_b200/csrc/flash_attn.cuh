@@ -257,8 +257,15 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           uint32_t u[32];
           tmem_ld32(tmem_base + lane_off + b * 128 + c4 * 32, u);
           tmem_wait_ld();
+          // two scores per instruction (packed multiply, round to nearest)
 #pragma unroll
-          for (int i = 0; i < 32; ++i) s[c4 * 32 + i] = __fmul_rn(__uint_as_float(u[i]), sl2);
+          for (int i = 0; i < 32; i += 2) {
+            const float2 v = __fmul2_rn(
+                make_float2(__uint_as_float(u[i]), __uint_as_float(u[i + 1])),
+                make_float2(sl2, sl2));
+            s[c4 * 32 + i] = v.x;
+            s[c4 * 32 + i + 1] = v.y;
+          }
         }
         tc_fence_before();
         mbar_arrive(&s_free[b]);
@@ -267,9 +274,18 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           for (int c = 0; c < 128; ++c)
             if (c > r) s[c] = -INFINITY;
         }
-        float mt = s[0];
+        // Row max as eight independent chains (max is exact in any order):
+        // one warp per SM sub-partition runs this, so a single 128-long
+        // dependency chain would stall it on every step.
+        float mx[8];
 #pragma unroll
-        for (int c = 1; c < 128; ++c) mt = fmaxf(mt, s[c]);
+        for (int i = 0; i < 8; ++i) mx[i] = s[i];
+#pragma unroll
+        for (int c = 8; c < 128; c += 8)
+#pragma unroll
+          for (int i = 0; i < 8; ++i) mx[i] = fmaxf(mx[i], s[c + i]);
+        const float mt = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
+                               fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
         if (j == 0) {
           m = mt;
         } else if (__any_sync(0xffffffffu, mt > m + kAttnRescale)) {
@@ -300,13 +316,16 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         const bool freed = mbar_wait(&p_free[b], ((t >> 1) & 1) ^ 1, abort_flag);
         if (!__all_sync(0xffffffffu, freed)) { ok = false; break; }
         uint8_t* prow = smem + kAttnOffP + b * kAttnTile + r * 128;
+        // The tile's row sum in eight partial sums (key c into sum c % 8),
+        // added to l at the end: eight short chains instead of one long one.
+        float ls[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
         for (int c = 0; c < 16; ++c) {  // 16 chunks of 8 keys
           float e[8];
 #pragma unroll
           for (int i = 0; i < 8; ++i) {
             e[i] = ex2_approx(s[c * 8 + i] - m);
-            l += e[i];
+            ls[i] += e[i];
           }
           uint4 v;
           v.x = pack_bf16x2(e[0], e[1]);
@@ -316,6 +335,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           const int half = c >> 3, ch = c & 7;
           *reinterpret_cast<uint4*>(prow + half * kAttnHalf + ((ch ^ (r & 7)) << 4)) = v;
         }
+        l += ((ls[0] + ls[1]) + (ls[2] + ls[3])) + ((ls[4] + ls[5]) + (ls[6] + ls[7]));
         fence_async_smem();
         tc_fence_before();  // orders a rescale's tcgen05.st before the PV
         mbar_arrive(&p_full[b]);

@@ -12,14 +12,16 @@
 namespace kvm {
 namespace {
 
+// tb2: B's map with BN / 2-row boxes, read only for half-width items of a
+// K-major B (p.split_tiles > 0); other launches pass tb again.
 template <int BN, int STAGES, bool B_MN, int EPI>
-int launch(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p,
-           int grid, cudaStream_t st) {
+int launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tb2,
+           const GemmParams& p, int grid, cudaStream_t st) {
   auto kern = gemm_bf16_kernel<BN, STAGES, B_MN, EPI>;
   constexpr size_t smem = gemm_smem_bytes<BN, STAGES>();
   KVM_CUDA_TRY(cudaFuncSetAttribute(
       kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
-  kern<<<grid, kGemmThreads, smem, st>>>(ta, tb, p);
+  kern<<<grid, kGemmThreads, smem, st>>>(ta, tb, tb2, p);
   KVM_CUDA_TRY(cudaGetLastError());
   return KVM_OK;
 }
@@ -177,10 +179,16 @@ extern "C" int kvm_sm100_gemm_bf16(const void* A, int64_t lda, const void* B,
   const bool narrow = !wide && 2LL * m_tiles * cdiv(N, 128) <= dev->sm_count;
   const int BN = wide ? 256 : narrow ? 64 : 128;
   const int tiles = m_tiles * cdiv(N, BN);
+  // A last wave of whole tiles on at most half of the SMs runs as twice as
+  // many half-width items instead (4096 x 4096 outputs in 128 x 256 tiles:
+  // 512 tiles = 3 waves + 68, so 3.5 tile times instead of 4).
+  const int tail = tiles % dev->sm_count;
+  if (BN >= 128 && tiles > dev->sm_count && tail > 0 && 2 * tail <= dev->sm_count)
+    p.split_tiles = tail;
   const int grid = tiles < dev->sm_count ? tiles : dev->sm_count;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
 
-  CUtensorMap ta, tb;
+  CUtensorMap ta, tb, tb2;
   KVM_TRY(encode_tmap_2d(&ta, A, K, M, lda * 2, kGemmBK, kGemmBM,
                          CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
                          CU_TENSOR_MAP_SWIZZLE_128B));
@@ -188,31 +196,37 @@ extern "C" int kvm_sm100_gemm_bf16(const void* A, int64_t lda, const void* B,
     KVM_TRY(encode_tmap_2d(&tb, B, K, N, ldb * 2, kGemmBK, BN,
                            CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
                            CU_TENSOR_MAP_SWIZZLE_128B));
+    tb2 = tb;
+    if (p.split_tiles > 0)
+      KVM_TRY(encode_tmap_2d(&tb2, B, K, N, ldb * 2, kGemmBK, BN / 2,
+                             CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
+                             CU_TENSOR_MAP_SWIZZLE_128B));
   } else {
     if (N % 8 != 0)
       return fail(KVM_ERR_INVALID_ARG, "gemm: [K,N] B needs N % 8 == 0");
     KVM_TRY(encode_tmap_2d(&tb, B, N, K, ldb * 2, 64, kGemmBK,
                            CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
                            CU_TENSOR_MAP_SWIZZLE_128B));
+    tb2 = tb;
   }
   const bool mn = b_layout == KVM_B_KN;
   const bool f32 = out_dtype == KVM_F32;
   if (wide) {
-    if (!mn && !f32) return launch<256, 4, false, kEpiBf16>(ta, tb, p, grid, st);
-    if (!mn && f32) return launch<256, 4, false, kEpiF32>(ta, tb, p, grid, st);
-    if (mn && !f32) return launch<256, 4, true, kEpiBf16>(ta, tb, p, grid, st);
-    return launch<256, 4, true, kEpiF32>(ta, tb, p, grid, st);
+    if (!mn && !f32) return launch<256, 4, false, kEpiBf16>(ta, tb, tb2, p, grid, st);
+    if (!mn && f32) return launch<256, 4, false, kEpiF32>(ta, tb, tb2, p, grid, st);
+    if (mn && !f32) return launch<256, 4, true, kEpiBf16>(ta, tb, tb2, p, grid, st);
+    return launch<256, 4, true, kEpiF32>(ta, tb, tb2, p, grid, st);
   }
   if (narrow) {
-    if (!mn && !f32) return launch<64, 8, false, kEpiBf16>(ta, tb, p, grid, st);
-    if (!mn && f32) return launch<64, 8, false, kEpiF32>(ta, tb, p, grid, st);
-    if (mn && !f32) return launch<64, 8, true, kEpiBf16>(ta, tb, p, grid, st);
-    return launch<64, 8, true, kEpiF32>(ta, tb, p, grid, st);
+    if (!mn && !f32) return launch<64, 8, false, kEpiBf16>(ta, tb, tb2, p, grid, st);
+    if (!mn && f32) return launch<64, 8, false, kEpiF32>(ta, tb, tb2, p, grid, st);
+    if (mn && !f32) return launch<64, 8, true, kEpiBf16>(ta, tb, tb2, p, grid, st);
+    return launch<64, 8, true, kEpiF32>(ta, tb, tb2, p, grid, st);
   }
-  if (!mn && !f32) return launch<128, 6, false, kEpiBf16>(ta, tb, p, grid, st);
-  if (!mn && f32) return launch<128, 6, false, kEpiF32>(ta, tb, p, grid, st);
-  if (mn && !f32) return launch<128, 6, true, kEpiBf16>(ta, tb, p, grid, st);
-  return launch<128, 6, true, kEpiF32>(ta, tb, p, grid, st);
+  if (!mn && !f32) return launch<128, 6, false, kEpiBf16>(ta, tb, tb2, p, grid, st);
+  if (!mn && f32) return launch<128, 6, false, kEpiF32>(ta, tb, tb2, p, grid, st);
+  if (mn && !f32) return launch<128, 6, true, kEpiBf16>(ta, tb, tb2, p, grid, st);
+  return launch<128, 6, true, kEpiF32>(ta, tb, tb2, p, grid, st);
 }
 
 // Shared body of the dense and grouped SiLU-gate / plain grouped launches.
@@ -269,8 +283,8 @@ static int grouped_impl(const void* A, long long lda, const void* B, void* D,
                          BN, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
                          CU_TENSOR_MAP_SWIZZLE_128B));
   if (epilogue == kEpiSilu)
-    return launch<BN, 4, false, kEpiSilu>(ta, tb, p, grid, st);
-  return launch<BN, 4, false, kEpiBf16>(ta, tb, p, grid, st);
+    return launch<BN, 4, false, kEpiSilu>(ta, tb, tb, p, grid, st);
+  return launch<BN, 4, false, kEpiBf16>(ta, tb, tb, p, grid, st);
 }
 
 extern "C" int kvm_sm100_gemm_bf16_silu_gate(const void* A, int64_t lda,
@@ -333,6 +347,6 @@ extern "C" int kvm_sm100_moe_router_topk(const void* x, const void* Wr,
   KVM_TRY(encode_tmap_2d(&tb, Wr, H, E, (uint64_t)H * 2, kGemmBK, 64,  // rows >= E read 0
                          CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
                          CU_TENSOR_MAP_SWIZZLE_128B));
-  return launch<64, 8, false, kEpiRouter>(ta, tb, p, grid,
+  return launch<64, 8, false, kEpiRouter>(ta, tb, tb, p, grid,
                                           static_cast<cudaStream_t>(stream));
 }

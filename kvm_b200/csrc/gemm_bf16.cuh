@@ -49,6 +49,8 @@ struct GemmParams {
   float* topk_w;
   int top_k;
   int* status;           // device status word
+  int split_tiles;       // the last split_tiles tiles run as two half-width
+                         // items each (BN >= 128; 0: none)
 };
 
 // Where one output tile's operands and results live.
@@ -57,6 +59,7 @@ struct GemmTile {
   int a_x, a_y;             // A box at K block kb: (a_x + kb*BK, a_y)
   int b_x, b_y;             // B: K-major (b_x + kb*BK, b_y); MN-major (b_x, b_y + kb*BK)
   int g;
+  int nb;                   // columns of this item: BN, or BN / 2 for a half
 };
 
 template <int BN>
@@ -153,14 +156,22 @@ __device__ __forceinline__ void store_row32(void* dst, const void* crow,
   }
 }
 
+// Work items: tile t for t below the split point; past it, each remaining
+// tile as two items of BN / 2 columns (first half, then second). When the
+// last wave of whole tiles would occupy at most half of the SMs, splitting it
+// lets the CTAs finish together. tmB2 is B's tensor map with BN / 2-row boxes
+// (K-major B; MN-major B loads 64-column boxes and ignores it).
 template <int BN, int STAGES, bool B_MN, int EPI>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA,
                      const __grid_constant__ CUtensorMap tmB,
+                     const __grid_constant__ CUtensorMap tmB2,
                      const GemmParams p) {
   using S = GemmSmem<BN>;
   constexpr int BM = kGemmBM, BK = kGemmBK;
   constexpr uint32_t kIdesc = idesc_bf16(BM, BN, 0, B_MN ? 1 : 0);
+  constexpr uint32_t kIdescHalf = idesc_bf16(BM, BN / 2, 0, B_MN ? 1 : 0);
+  constexpr bool kCanSplit = BN >= 128;
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
@@ -217,6 +228,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
+    if (!B_MN && kCanSplit && p.split_tiles > 0) tma_prefetch_desc(&tmB2);
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, S::kTmemCols);
@@ -227,6 +239,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   const int total_tiles = g_pref[G];
+  const int split_first =
+      kCanSplit ? total_tiles - min(max(p.split_tiles, 0), total_tiles) : total_tiles;
+  const int total_items = 2 * total_tiles - split_first;
 
   auto map_tile = [&](int t) {
     int lo = 0, hi = G - 1;  // largest g with g_pref[g] <= t
@@ -248,6 +263,18 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     tl.a_y = tl.row0;
     tl.b_x = B_MN ? tl.col0 : 0;
     tl.b_y = g * p.b_group_rows + (B_MN ? 0 : tl.col0);
+    tl.nb = BN;
+    return tl;
+  };
+  auto map_item = [&](int i) {
+    if (i < split_first) return map_tile(i);
+    const int u = i - split_first;
+    GemmTile tl = map_tile(split_first + (u >> 1));
+    tl.nb = BN / 2;
+    if (u & 1) {
+      tl.col0 += BN / 2;
+      if (B_MN) tl.b_x += BN / 2; else tl.b_y += BN / 2;
+    }
     return tl;
   };
 
@@ -261,23 +288,25 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 #pragma unroll
       for (int i = 0; i < STAGES; ++i) armed[i] = false;
       bool ok = true;
-      for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
-        const GemmTile tl = map_tile(t);
+      for (int t = blockIdx.x; t < total_items && ok; t += gridDim.x) {
+        const GemmTile tl = map_item(t);
+        const bool whole = tl.nb == BN;
         for (int kb = 0; kb < k_blocks; ++kb) {
           if (!mbar_wait(&empty[s], ph ^ 1, abort_flag)) { ok = false; break; }
           uint8_t* a_dst = smem + s * S::kStageBytes;
           uint8_t* b_dst = a_dst + S::kABytes;
-          mbar_arrive_expect_tx(&full[s], S::kStageBytes);
+          mbar_arrive_expect_tx(&full[s], S::kABytes + tl.nb * (BK * 2));
           armed[s] = true;
           armed_ph[s] = ph;
           tma_load_2d(a_dst, &tmA, &full[s], tl.a_x + kb * BK, tl.a_y);
           if (!B_MN) {
-            tma_load_2d(b_dst, &tmB, &full[s], tl.b_x + kb * BK, tl.b_y);
+            tma_load_2d(b_dst, whole ? &tmB : &tmB2, &full[s], tl.b_x + kb * BK, tl.b_y);
           } else {
 #pragma unroll
             for (int j = 0; j < BN / 64; ++j)
-              tma_load_2d(b_dst + j * (64 * BK * 2), &tmB, &full[s],
-                          tl.b_x + j * 64, tl.b_y + kb * BK);
+              if (j * 64 < tl.nb)
+                tma_load_2d(b_dst + j * (64 * BK * 2), &tmB, &full[s],
+                            tl.b_x + j * 64, tl.b_y + kb * BK);
           }
           if (++s == STAGES) { s = 0; ph ^= 1; }
         }
@@ -296,7 +325,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       uint32_t ph = 0;
       int it = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
+      for (int t = blockIdx.x; t < total_items && ok; t += gridDim.x) {
+        const uint32_t idesc = t < split_first ? kIdesc : kIdescHalf;
         const int acc = it & 1;
         const uint32_t aph = (it >> 1) & 1;
         ++it;
@@ -314,7 +344,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             const uint64_t bdesc =
                 B_MN ? sdesc_sw128(b_addr + k * 2048, 64 * BK * 2, 1024)
                      : sdesc_sw128(b_addr + k * 32, 0, 1024);
-            mma_f16_ss(d_tmem, adesc, bdesc, kIdesc, (kb | k) != 0);
+            mma_f16_ss(d_tmem, adesc, bdesc, idesc, (kb | k) != 0);
           }
           mma_commit(&empty[s]);
           if (++s == STAGES) { s = 0; ph ^= 1; }
@@ -331,8 +361,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const int q = warp & 3;  // TMEM lane quarter this warp may access
     const int r_in_tile = q * 32 + lane;
     int it = 0;
-    for (int t = blockIdx.x; t < total_tiles; t += gridDim.x) {
-      const GemmTile tl = map_tile(t);
+    for (int t = blockIdx.x; t < total_items; t += gridDim.x) {
+      const GemmTile tl = map_item(t);
       const int row0 = tl.row0, row_end = tl.row_end, col0 = tl.col0;
       const int acc = it & 1;
       const uint32_t aph = (it >> 1) & 1;
@@ -350,7 +380,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         constexpr bool F32 = EPI == kEpiF32;
         constexpr int ES = F32 ? 4 : 2;
 #pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
+        for (int c = 0; c < tl.nb / 32; ++c) {
           uint32_t r[32];
           tmem_ld32(t_row + c * 32, r);
           tmem_wait_ld();

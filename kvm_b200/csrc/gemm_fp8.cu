@@ -271,9 +271,17 @@ __global__ void __launch_bounds__(f8_threads(EW), 1)
         tc_fence_before();
         mbar_arrive(&tempty[b]);
         const float sc = __shfl_sync(0xffffffffu, sc_lane, j32);
+        // Two columns per instruction (packed fp32 FMA, round to nearest:
+        // the same result as two scalar fmaf_rn).
+        const float2 sc2 = make_float2(sc, sc);
 #pragma unroll
-        for (int j = 0; j < COLS; ++j)
-          acc[j] = __fmaf_rn(__uint_as_float(v[j]), sc, acc[j]);
+        for (int j = 0; j < COLS; j += 2) {
+          const float2 r = __ffma2_rn(
+              make_float2(__uint_as_float(v[j]), __uint_as_float(v[j + 1])), sc2,
+              make_float2(acc[j], acc[j + 1]));
+          acc[j] = r.x;
+          acc[j + 1] = r.y;
+        }
       }
       if (!ok) break;
       const bool whole = kb0 == 0 && kb1 == kbs;

@@ -21,6 +21,10 @@ SHAPES = [
     (1, 64, 8),          # tiny
     (1024, 1024, 1024),  # the single-matmul graph's shape
     (4736, 2048, 256),   # more tiles than SMs: persistent loop, 2 TMEM buffers
+    # On 148 SMs the last wave of these runs as half-width items:
+    (1280, 1920, 256),   # 150 tiles of 128 x 128: the last 2 as 4 halves of 64
+    (4096, 2560, 128),   # 320 tiles of 128 x 256: the last 24 as 48 halves
+    (4000, 2408, 200),   # ragged; the very last half lies wholly past N
 ]
 
 
@@ -45,9 +49,9 @@ def test_matmul_bf16(cuda, M, N, K, layout):
 
 
 @pytest.mark.parametrize("layout", ["nk", "kn"])
-def test_gemm_f32_with_addend(cuda, layout):
+@pytest.mark.parametrize("M,N,K", [(384, 640, 512), (1280, 1920, 256)])
+def test_gemm_f32_with_addend(cuda, layout, M, N, K):
     rng = np.random.default_rng(11)
-    M, N, K = 384, 640, 512
     a = oracle.normal_bf16(rng, (M, K))
     b = oracle.normal_bf16(rng, (K, N) if layout == "kn" else (N, K))
     c = rng.standard_normal((M, N), dtype=np.float32)
