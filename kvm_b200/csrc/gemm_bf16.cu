@@ -338,10 +338,15 @@ extern "C" int kvm_sm100_moe_router_topk(const void* x, const void* Wr,
   p.D = logits; p.ldd = E;
   p.logits = logits; p.topk_idx = topk_idx; p.topk_w = topk_w; p.top_k = k;
   p.status = dev->status;
-  const int tiles = cdiv(T, kGemmBM);
+  // Rows per tile: enough tiles to give every SM one (8192 tokens on 148
+  // SMs: 147 tiles of 56 rows), at least 32 rows and at most 128.
+  int tr = (cdiv(T, dev->sm_count) + 7) & ~7;
+  tr = tr < 32 ? 32 : tr > kGemmBM ? kGemmBM : tr;
+  p.tile_rows = tr;
+  const int tiles = cdiv(T, tr);
   const int grid = tiles < dev->sm_count ? tiles : dev->sm_count;
   CUtensorMap ta, tb;
-  KVM_TRY(encode_tmap_2d(&ta, x, H, T, (uint64_t)H * 2, kGemmBK, kGemmBM,
+  KVM_TRY(encode_tmap_2d(&ta, x, H, T, (uint64_t)H * 2, kGemmBK, tr,
                          CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
                          CU_TENSOR_MAP_SWIZZLE_128B));
   KVM_TRY(encode_tmap_2d(&tb, Wr, H, E, (uint64_t)H * 2, kGemmBK, 64,  // rows >= E read 0

@@ -51,6 +51,8 @@ struct GemmParams {
   int* status;           // device status word
   int split_tiles;       // the last split_tiles tiles run as two half-width
                          // items each (BN >= 128; 0: none)
+  int tile_rows;         // router only: rows per tile, a multiple of 8 in
+                         // [8, 128] (0: 128); A's tensor map box has as many
 };
 
 // Where one output tile's operands and results live.
@@ -172,6 +174,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   constexpr uint32_t kIdesc = idesc_bf16(BM, BN, 0, B_MN ? 1 : 0);
   constexpr uint32_t kIdescHalf = idesc_bf16(BM, BN / 2, 0, B_MN ? 1 : 0);
   constexpr bool kCanSplit = BN >= 128;
+  // Rows per tile. The router takes fewer than 128 so that its tiles fill the
+  // SMs (it streams x once, and a CTA's share of the bytes sets its time);
+  // the MMA stays M = 128 and TMEM lanes at or past TR, whose A rows in
+  // shared memory the TMA never writes, are not read back.
+  const int TR = (EPI == kEpiRouter && p.tile_rows > 0) ? p.tile_rows : BM;
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
@@ -207,7 +214,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         bad = true;
         hi = lo = 0;
       }
-      int mt = (hi - lo + BM - 1) / BM;
+      int mt = (hi - lo + TR - 1) / TR;
       g_mt[g] = mt;
       g_pref[g] = acc;
       acc += mt * n_tiles;
@@ -256,7 +263,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const int mi = local - nt * mt;
     GemmTile tl;
     tl.g = g;
-    tl.row0 = g_off[g] + mi * BM;
+    tl.row0 = g_off[g] + mi * TR;
     tl.row_end = g_off[g + 1];
     tl.col0 = nt * BN;
     tl.a_x = 0;
@@ -295,7 +302,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           if (!mbar_wait(&empty[s], ph ^ 1, abort_flag)) { ok = false; break; }
           uint8_t* a_dst = smem + s * S::kStageBytes;
           uint8_t* b_dst = a_dst + S::kABytes;
-          mbar_arrive_expect_tx(&full[s], S::kABytes + tl.nb * (BK * 2));
+          mbar_arrive_expect_tx(&full[s], TR * (BK * 2) + tl.nb * (BK * 2));
           armed[s] = true;
           armed_ph[s] = ph;
           tma_load_2d(a_dst, &tmA, &full[s], tl.a_x + kb * BK, tl.a_y);
@@ -374,7 +381,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
                              acc * BN;
       const int row = row0 + r_in_tile;
-      const bool row_ok = row < row_end;
+      const bool row_ok = row < row_end && r_in_tile < TR;
 
       if constexpr (EPI == kEpiBf16 || EPI == kEpiF32) {
         constexpr bool F32 = EPI == kEpiF32;
