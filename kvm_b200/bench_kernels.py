@@ -23,12 +23,31 @@ quantised per block to amax 448).
 from __future__ import annotations
 
 import json
+from pathlib import Path
 import statistics
 import time
 
 import torch
 
 from . import ops
+
+_PROFILES = Path(__file__).resolve().parents[1] / "profiles"
+
+
+def _traffic(profile: str):
+    """DRAM bytes (read + write) per launch of a line's dominant kernel, from
+    the `traffic_bytes_per_launch:` line of its committed ncu summary, or
+    None when there is none."""
+    p = _PROFILES / f"{profile}.md"
+    if not p.exists():
+        return None
+    for line in p.read_text().splitlines():
+        if line.strip().startswith("traffic_bytes_per_launch:"):
+            try:
+                return float(line.split(":", 1)[1].split()[0])
+            except (ValueError, IndexError):
+                return None
+    return None
 
 
 def _time(fn, steps, warmup, flush=None):
@@ -212,7 +231,8 @@ def run_attn(args, peaks, ClockSampler, dev, g) -> int:
           config={"workload": f"causal_gqa_attention_B{B}_L{L}_HQ{HQ}_HKV{HKV}_hd128",
                   "l2": "168 MB of q/k/v > L2"},
           roofline={"bound": "tensor", "achieved": tf, "peak": peaks["bf16"],
-                    "unit": "TFLOP/s", "frac": tf / peaks["bf16"], "traffic": None,
+                    "unit": "TFLOP/s", "frac": tf / peaks["bf16"],
+                    "traffic": _traffic("attn_fwd_B4_L2048_HQ64"),
                     "kernel": "attn_fwd_kernel"},
           gpu_launches=steps)
     return 0
@@ -266,7 +286,8 @@ def run_decode(args, peaks, ClockSampler, dev, g) -> int:
                   "kv_bytes_per_step": kv_bytes, "tflops": flop / (ms / 1e3) / 1e12,
                   "l2": f"{kv_bytes / 1e9:.2f} GB of K/V per step > L2"},
           roofline={"bound": "hbm", "achieved": gbs, "peak": peaks["hbm"], "unit": "GB/s",
-                    "frac": gbs / peaks["hbm"], "traffic": None,
+                    "frac": gbs / peaks["hbm"],
+                    "traffic": _traffic("paged_decode_S16_ctx4096") if S == 64 else None,
                     "kernel": "decode_attn_kernel + combine + kvcache.write"},
           gpu_launches=3 * steps)
     return 0
@@ -329,7 +350,9 @@ def run_ew(args, peaks, ClockSampler, dev, g) -> int:
                                             "interpreter_ms": ms_norm_i,
                                             "l2": "flushed before each launch"}},
           roofline={"bound": "hbm", "achieved": gbs, "peak": peaks["hbm"], "unit": "GB/s",
-                    "frac": gbs / peaks["hbm"], "traffic": None, "kernel": "kvm_ew (generated)"},
+                    "frac": gbs / peaks["hbm"],
+                    "traffic": _traffic("fused_elementwise_silu_8192x14336"),
+                    "kernel": "kvm_ew (generated)"},
           gpu_launches=steps)
     return 0
 
@@ -360,7 +383,8 @@ def run(args, peaks, ClockSampler) -> int:
               config={"workload": "bf16_matmul_1024x1024x1024",
                       "l2": "flushed before each launch (256 MB read)"},
               roofline={"bound": "tensor", "achieved": tf, "peak": peaks["bf16"],
-                        "unit": "TFLOP/s", "frac": tf / peaks["bf16"], "traffic": None},
+                        "unit": "TFLOP/s", "frac": tf / peaks["bf16"],
+                        "traffic": _traffic("gemm_bf16_1024x1024x1024")},
               gpu_launches=steps)
         return 0
     if args.workload == "decode":
@@ -403,7 +427,8 @@ def run(args, peaks, ClockSampler) -> int:
               config={"workload": "gated_mlp_T4096_H4096_F14336", "l2": "weights 352 MB > L2"},
               roofline={"bound": "tensor", "achieved": gu_tf, "peak": peaks["bf16_sustained"],
                         "unit": "TFLOP/s", "frac": gu_tf / peaks["bf16_sustained"],
-                        "traffic": None, "kernel": "gate/up GEMM + fused SiLU-gate",
+                        "traffic": _traffic("gated_mlp_T4096_H4096_F14336"),
+                        "kernel": "gate/up GEMM + fused SiLU-gate",
                         "ms": t_gu},
               gpu_launches=3 * steps)
         return 0
@@ -446,6 +471,7 @@ def run(args, peaks, ClockSampler) -> int:
           config={"workload": "fp8_w8a8_blockscaled_K8192_N28672", "per_m": rows,
                   "fp8_peak_tflops": f"{fp8_peak:.0f} (2 x measured bf16)"},
           roofline={"bound": "hbm", "achieved": r16["gbs"], "peak": peaks["hbm"],
-                    "unit": "GB/s", "frac": r16["gbs"] / peaks["hbm"], "traffic": None},
+                    "unit": "GB/s", "frac": r16["gbs"] / peaks["hbm"],
+                    "traffic": _traffic("fp8_gemm_K8192_N28672")},
           gpu_launches=3 * steps)
     return 0
