@@ -26,8 +26,9 @@ def _weights(rng, E, H, F):
 
 @pytest.mark.parametrize("T,k,E", [(512, 2, 64), (1, 2, 64), (300, 1, 64), (129, 8, 64),
                                    (700, 2, 16), (64, 3, 5),
-                                   # tiles of 56 and 32 rows on 148 SMs, ragged last tile
-                                   (8192, 2, 64), (4099, 2, 64)])
+                                   # tiles of 56, 32 and 88 rows on 148 SMs, ragged
+                                   # last tiles
+                                   (8192, 2, 64), (4099, 2, 64), (12000, 2, 64)])
 def test_router_topk_bit_exact_given_logits(cuda, T, k, E):
     rng = np.random.default_rng(T + k)
     H = 256
