@@ -76,7 +76,12 @@ def make_plan(rank: int, world: int, experts: int, send_offsets, recv_counts) ->
 class CudaCompute:
     """Local compute of one rank on the sm_100a kernels."""
 
-    LAUNCHES = 8  # router 1, permute 3, scatter 1, grouped GEMMs 2, combine 1
+    @property
+    def LAUNCHES(self) -> int:
+        """Kernels per call on max_tokens tokens: router 1, permute 2 or 3,
+        scatter 1, grouped GEMMs 2, combine 1."""
+        from .moe import permute_launches
+        return 5 + permute_launches(self.max_tokens * self.k, self.E)
 
     def __init__(self, w_router, w13_local, w2_local, top_k, max_tokens, world):
         from ._lib import lib
@@ -84,6 +89,7 @@ class CudaCompute:
         self.E, self.H = w_router.shape
         self.F = w13_local.shape[1] // 2
         self.k = top_k
+        self.max_tokens = max_tokens
         dev = w_router.device
         T, k, E, H, F = max_tokens, top_k, self.E, self.H, self.F
         self.logits = torch.empty((T, E), dtype=torch.float32, device=dev)
@@ -218,13 +224,18 @@ class ExpertParallelMoE:
     Buffers that peers touch (receive rows, expert outputs, count matrix,
     flags) are allocated with kvm_sm100_ipc_alloc and mapped into every rank
     through CUDA IPC handles exchanged over the process group once, at
-    construction. A call launches 12 kernels on the current stream and never
-    synchronises with the host: route, permute (local), count exchange,
+    construction. A call launches 11 or 12 kernels (LAUNCHES_PER_CALL) on the
+    current stream and never synchronises with the host: route, permute (local), count exchange,
     dispatch (peer stores), wait, grouped GEMMs, signal, wait, combine (peer
     loads). Weak scaling: each rank brings `max_tokens` tokens at most.
     """
 
-    LAUNCHES_PER_CALL = 12
+    @property
+    def LAUNCHES_PER_CALL(self) -> int:
+        """route 1, permute 2 or 3, count exchange 1, dispatch 1, wait 1,
+        grouped GEMMs 2, signal 1, wait 1, combine 1."""
+        from .moe import permute_launches
+        return 9 + permute_launches(self.max_tokens * self.k, self.E)
 
     def __init__(self, w_router, w13, w2, *, top_k: int, max_tokens: int, rank: int,
                  world: int, group=None):

@@ -22,6 +22,15 @@ from . import ops
 from ._lib import call, lib
 
 
+def permute_launches(n_pairs: int, E: int) -> int:
+    """Kernels kvm_sm100_moe_permute launches for n_pairs (token, expert)
+    pairs: a count pass and a rank pass that also forms the offsets when the
+    per-block count matrix (ceil(n_pairs / 256) x E) has at most 16384
+    entries, else count, scan and rank."""
+    blocks = (n_pairs + 255) // 256
+    return 2 if blocks * E <= 16 * 1024 else 3
+
+
 def _out_buffer(out, own, T, H):
     if out is None:
         return own
@@ -127,5 +136,8 @@ class MoELayer:
              self.topk_w.data_ptr(), dst.data_ptr(), T, k, H, st)
         return dst[:T]
 
-    # Kernels one call launches (router 1, permute 3, scatter 1, GEMMs 2, combine 1).
-    LAUNCHES_PER_CALL = 8
+    @property
+    def LAUNCHES_PER_CALL(self) -> int:
+        """Kernels one call on max_tokens tokens launches: router 1, permute
+        2 or 3, scatter 1, grouped GEMMs 2, combine 1."""
+        return 5 + permute_launches(self.max_tokens * self.k, self.E)
