@@ -88,21 +88,47 @@ __global__ void __launch_bounds__(kPermChunk)
                         int* __restrict__ src_token, int n_chunks,
                         int* __restrict__ offsets) {
   constexpr int kWarps = kPermChunk / 32;
-  extern __shared__ int wcount[];  // [kWarps][E], then (FUSED) [2][E]
+  // [kWarps][E], then (FUSED) cbase [E], tot [E], two [max(kPermChunk, E)]
+  extern __shared__ int wcount[];
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  // this thread's pair, loaded before the prologue so the load overlaps it
+  const int i = blockIdx.x * kPermChunk + threadIdx.x;
+  int e = -1;
+  if (i < n) {
+    e = idx[i];
+    if (e < 0 || e >= E) e = -1;
+  }
   for (int x = threadIdx.x; x < kWarps * E; x += blockDim.x) wcount[x] = 0;
   int* cbase = wcount + kWarps * E;  // this chunk's base per expert
   if constexpr (FUSED) {
     int* tot = cbase + E;
-    for (int e = threadIdx.x; e < E; e += blockDim.x) {
+    int* part_before = tot + E;
+    int* part_all = part_before + (E > kPermChunk ? E : kPermChunk);
+    // Column sums of the count matrix by G row groups x E experts, so every
+    // thread of the block loads (G = kPermChunk / E rows apart), then the G
+    // partial sums per expert are added (integers: any order is exact).
+    const int G = E <= kPermChunk ? kPermChunk / E : 1;
+    for (int x = threadIdx.x; x < G * E; x += blockDim.x) {
+      const int ex = x % E, g = x / E;
       int before = 0, all = 0;
-      for (int c = 0; c < n_chunks; ++c) {
-        const int v = base[static_cast<long long>(c) * E + e];
+#pragma unroll 8
+      for (int c = g; c < n_chunks; c += G) {
+        const int v = base[static_cast<long long>(c) * E + ex];
         before += c < static_cast<int>(blockIdx.x) ? v : 0;
         all += v;
       }
-      cbase[e] = before;
-      tot[e] = all;
+      part_before[x] = before;
+      part_all[x] = all;
+    }
+    __syncthreads();
+    for (int ex = threadIdx.x; ex < E; ex += blockDim.x) {
+      int before = 0, all = 0;
+      for (int g = 0; g < G; ++g) {
+        before += part_before[g * E + ex];
+        all += part_all[g * E + ex];
+      }
+      cbase[ex] = before;
+      tot[ex] = all;
     }
     __syncthreads();
     // exclusive scan of the expert totals, in place (Hillis-Steele on E <= 1024)
@@ -110,32 +136,26 @@ __global__ void __launch_bounds__(kPermChunk)
       int add[4];
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        const int e = threadIdx.x + j * kPermChunk;
-        add[j] = (e < E && e >= d) ? tot[e - d] : 0;
+        const int ex = threadIdx.x + j * kPermChunk;
+        add[j] = (ex < E && ex >= d) ? tot[ex - d] : 0;
       }
       __syncthreads();
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        const int e = threadIdx.x + j * kPermChunk;
-        if (e < E) tot[e] += add[j];
+        const int ex = threadIdx.x + j * kPermChunk;
+        if (ex < E) tot[ex] += add[j];
       }
       __syncthreads();
     }
     // tot is now inclusive: offsets[e] = tot[e - 1]
-    for (int e = threadIdx.x; e < E; e += blockDim.x) {
-      const int off = e > 0 ? tot[e - 1] : 0;
-      cbase[e] += off;
-      if (blockIdx.x == 0) offsets[e] = off;
+    for (int ex = threadIdx.x; ex < E; ex += blockDim.x) {
+      const int off = ex > 0 ? tot[ex - 1] : 0;
+      cbase[ex] += off;
+      if (blockIdx.x == 0) offsets[ex] = off;
     }
     if (blockIdx.x == 0 && threadIdx.x == 0) offsets[E] = tot[E - 1];
   }
   __syncthreads();
-  const int i = blockIdx.x * kPermChunk + threadIdx.x;
-  int e = -1;
-  if (i < n) {
-    e = idx[i];
-    if (e < 0 || e >= E) e = -1;
-  }
   const unsigned peers = __match_any_sync(0xffffffffu, e);
   const unsigned lt = (1u << lane) - 1u;
   const int rank_in_warp = __popc(peers & lt);
@@ -292,7 +312,8 @@ int launch_permute(const int32_t* topk_idx, int n, int k, int E, int nc, int* co
   KVM_CUDA_TRY(cudaGetLastError());
   const size_t rank_smem = (kPermChunk / 32) * E * sizeof(int);
   if (static_cast<long long>(nc) * E <= 16 * 1024) {
-    const size_t smem = rank_smem + 2 * E * sizeof(int);
+    const size_t smem =
+        rank_smem + (2 * E + 2 * (E > kPermChunk ? E : kPermChunk)) * sizeof(int);
     if (smem > 48 * 1024)
       KVM_CUDA_TRY(cudaFuncSetAttribute(permute_rank_kernel<true>,
                                         cudaFuncAttributeMaxDynamicSharedMemorySize,

@@ -57,7 +57,11 @@ def test_router_ties_take_lower_expert(cuda):
 
 @pytest.mark.parametrize("T,k,E,skew", [(4096, 2, 64, False), (1000, 2, 64, True),
                                         (7, 3, 64, False), (2048, 8, 16, False),
-                                        (513, 1, 1, False)])
+                                        (513, 1, 1, False),
+                                        # more experts than threads per block
+                                        (600, 2, 300, False),
+                                        # count matrix over 16K cells: separate scan
+                                        (40000, 2, 64, False)])
 def test_permute_and_scatter_bit_exact(cuda, T, k, E, skew):
     rng = np.random.default_rng(T * 3 + k)
     if skew:   # most pairs on two experts, many experts empty
