@@ -11,8 +11,8 @@
 lowering of dispatch/combine is src/device/device.cpp:143-147.)
 
 All buffers are allocated once, at construction, for ``max_tokens``; a call
-launches eight kernels on the current stream and allocates nothing, so the
-call can be captured in a CUDA graph.
+launches seven or eight kernels (LAUNCHES_PER_CALL) on the current stream and
+allocates nothing, so the call can be captured in a CUDA graph.
 """
 from __future__ import annotations
 
