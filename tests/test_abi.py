@@ -55,6 +55,16 @@ def test_permute_workspace_size():
     assert L.kvm_sm100_moe_permute_workspace(8192, 2, 64) == 2 * 64 * 64 * 4
 
 
+def test_permute_launch_count():
+    """The permutation folds its scan into the rank kernel (2 launches) while
+    the per-block count matrix has at most 16 K cells, else 3."""
+    from kvm_b200.moe import permute_launches
+    assert permute_launches(8192 * 2, 64) == 2          # 64 x 64 cells
+    assert permute_launches(256 * 256, 64) == 2         # exactly 16 K cells
+    assert permute_launches(256 * 256 + 1, 64) == 3
+    assert permute_launches(40000 * 2, 64) == 3
+
+
 def test_product_code_never_imports_the_oracle():
     offenders = []
     for p in (ROOT / "kvm_b200").rglob("*"):
