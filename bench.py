@@ -216,6 +216,90 @@ def cpu_job(name, args, kw, units, unit, sample, max_reps, min_s=3.0):
             "kind": "port", "sample": f"{sample}, x{done} in {dt:.1f} s"}
 
 
+# DRAM bytes (read + write) of one launch of the dominant kernel, from an ncu
+# capture, with where the figure comes from (the summary file under profiles/
+# gives the command that produced it).
+GATE_UP_TRAFFIC = {
+    "bytes": 1684342784.0,
+    "src": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one gemm_pair_kernel<2> "
+           "launch on the T2048_E16 profiling case, scaled x4 to T8192_E64 (weights and "
+           "token rows both scale by 4): profiles/moe_pair_gemm_T8192.md",
+}
+
+
+def roofline_entry(name, ms, flop=None, nbytes=None, pk=None, peak_kind="burst"):
+    """One kernel's roofline: the binding bound (tensor if FLOP / peak takes
+    longer than bytes / HBM peak, else HBM) and achieved = work / ms."""
+    bf16 = pk["bf16_sustained"] if peak_kind == "sustained" else pk["bf16"]
+    t_tensor = flop / (bf16 * 1e12) if flop else 0.0
+    t_hbm = nbytes / (pk["hbm"] * 1e9) if nbytes else 0.0
+    t = ms / 1e3
+    if t_tensor >= t_hbm:
+        e = {"bound": "tensor", "achieved": flop / t / 1e12, "peak": bf16, "unit": "TFLOP/s"}
+        src = f"{pk['src']} ({peak_kind} bf16)"
+    else:
+        e = {"bound": "hbm", "achieved": nbytes / t / 1e9, "peak": pk["hbm"], "unit": "GB/s"}
+        src = f"{pk['src']} (hbm copy)"
+    e["frac"] = e["achieved"] / e["peak"]
+    e.update({"kernel": name, "ms": ms, "flop": flop, "bytes": nbytes, "peak_src": src})
+    return e
+
+
+def layer_rooflines(phases: dict, world: int, pk: dict, peak_kind: str) -> list:
+    """Roofline entries of the layer's kernels from their mean event times.
+    Algorithmic work per launch (T tokens of this rank, k slots, E experts,
+    E/P local, R = rows the rank's experts receive = T*k on average):
+      router   x [T,H] + Wr [E,H] read, logits [T,E] f32 + top-k [T,k] (i32+f32)
+               written; 2*T*H*E FLOP (HBM-bound)
+      gate_up  2*R*2F*H FLOP; W13 [E/P,2F,H] + rows [R,H] read, H [R,F] written
+      down     2*R*H*F FLOP;  W2 [E/P,H,F] + H [R,F] read, Y [R,H] written
+      scatter  x [T,H] read, [T*k,H] written
+      combine  [T*k,H] read, out [T,H] written
+      ep_dispatch / ep_combine: the same bytes as scatter / combine, (P-1)/P of
+               them over NVLink."""
+    T, H, E, F, k = TOKENS, HIDDEN, EXPERTS, FFN, TOP_K
+    R = T * k
+    el = E // world
+    work = {
+        "router": (2.0 * T * H * E, T * H * 2 + E * H * 2 + T * E * 4 + T * k * 8),
+        "gate_up": (2.0 * R * 2 * F * H, el * 2 * F * H * 2 + R * H * 2 + R * F * 2),
+        "down": (2.0 * R * H * F, el * H * F * 2 + R * F * 2 + R * H * 2),
+        "scatter": (None, T * H * 2 + R * H * 2),
+        "combine": (None, R * H * 2 + T * H * 2),
+        "ep_dispatch": (None, T * H * 2 + R * H * 2),
+        "ep_combine": (None, R * H * 2 + T * H * 2),
+    }
+    out = []
+    for name, (flop, nbytes) in work.items():
+        if name in phases and phases[name] > 0:
+            out.append(roofline_entry(name, phases[name], flop, nbytes, pk, peak_kind))
+    return out
+
+
+def ep_parity(layer, x, wr, w13, w2, rank, world, n=256):
+    """Bit-exact check of the expert-parallel layer: the first n tokens of
+    every rank's batch, gathered on rank 0, through the one-GPU layer (which
+    holds all E experts). Every rank takes part in the gather; rank 0 returns
+    the verdict, the others None."""
+    import torch
+    import torch.distributed as dist
+    from kvm_b200.moe import MoELayer
+    out = layer(x)[:n].contiguous()
+    xs = x[:n].contiguous()
+    gx = [torch.empty_like(xs) for _ in range(world)]
+    gy = [torch.empty_like(out) for _ in range(world)]
+    dist.all_gather(gx, xs)
+    dist.all_gather(gy, out)
+    if rank != 0:
+        return None
+    ref_layer = MoELayer(wr, w13, w2, TOP_K, n * world)
+    ref = ref_layer(torch.cat(gx))
+    got = torch.cat(gy)
+    same = torch.equal(ref.view(torch.int16), got.view(torch.int16))
+    diff = (ref.float() - got.float()).abs().max().item()
+    return {"bitexact": bool(same), "tokens_checked": n * world, "max_abs_diff": diff}
+
+
 def run_ours(args) -> int:
     import torch
     import torch.distributed as dist
@@ -236,6 +320,7 @@ def run_ours(args) -> int:
 
     from kvm_b200 import _lib
     from kvm_b200.moe import MoELayer
+    from kvm_b200.timing import PhaseProbe
 
     gen = torch.Generator(device=dev)
     gen.manual_seed(0)
@@ -247,14 +332,15 @@ def run_ours(args) -> int:
         from kvm_b200.ep import ExpertParallelMoE
         layer = ExpertParallelMoE(wr, w13, w2, top_k=TOP_K, max_tokens=TOKENS,
                                   rank=rank, world=world)
+        if rank != 0:      # rank 0 keeps all experts for the parity check
+            w13 = w2 = None
     else:
         layer = MoELayer(wr, w13, w2, TOP_K, TOKENS)
-    del w13, w2
+        w13 = w2 = None
     torch.cuda.synchronize()
 
     stream = torch.cuda.current_stream()
-    probe = {"start": [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)],
-             "end": [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]}
+    probe = PhaseProbe(args.steps, layer.PHASES)
 
     def barrier():
         if world > 1:
@@ -274,18 +360,20 @@ def run_ours(args) -> int:
         wall0 = time.time()
         ev0.record(stream)
         for i in range(args.steps):
-            layer(x, probe=(probe["start"][i], probe["end"][i]))
+            layer(x, probe=probe.next_call())
         ev1.record(stream)
         torch.cuda.synchronize()
         wall1 = time.time()
         barrier()
     _lib.device_status()
     ms = ev0.elapsed_time(ev1)
-    gemm_ms = statistics.mean(s.elapsed_time(e) for s, e in zip(probe["start"], probe["end"]))
+    phases = probe.mean_ms()
     if world > 1:
-        t = torch.tensor([ms, gemm_ms], dtype=torch.float64, device=dev)
+        names = list(phases)
+        t = torch.tensor([ms] + [phases[n] for n in names], dtype=torch.float64, device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms, gemm_ms = float(t[0]), float(t[1])
+        ms = float(t[0])
+        phases = {n: float(v) for n, v in zip(names, t[1:].tolist())}
     ms_per_step = ms / args.steps
     value = TOKENS * world * args.steps / (ms / 1e3)
 
@@ -319,28 +407,23 @@ def run_ours(args) -> int:
     e2e_value = TOKENS * world * e2e_steps / (e2e_ms / 1e3)
     _lib.device_status()
 
-    # ---- roofline of the dominant kernel: grouped gate/up GEMM + SiLU-gate
+    parity = None
+    if world > 1:
+        parity = ep_parity(layer, x, wr, w13, w2, rank, world)
+        _lib.device_status()
+
+    # ---- roofline of the dominant kernel (grouped gate/up GEMM + SiLU-gate)
+    # and of the others; the burst bf16 peak applies to a timed region of
+    # under 2 s, the sustained one (power-capped clocks) to longer ones
     pk = peaks()
-    rows = TOKENS * TOP_K
-    flops = 2.0 * rows * (2 * FFN) * HIDDEN
-    n_local_experts = EXPERTS // world
-    bytes_alg = (n_local_experts * 2 * FFN * HIDDEN * 2      # W13 read once
-                 + rows * HIDDEN * 2 + rows * FFN * 2)        # A read, H written
-    t_s = gemm_ms / 1e3
-    t_tensor = flops / (pk["bf16_sustained"] * 1e12)
-    t_hbm = bytes_alg / (pk["hbm"] * 1e9)
-    traffic = profile_traffic()
-    if t_tensor >= t_hbm:
-        roof = {"bound": "tensor", "achieved": flops / t_s / 1e12,
-                "peak": pk["bf16_sustained"], "unit": "TFLOP/s"}
-    else:
-        roof = {"bound": "hbm", "achieved": bytes_alg / t_s / 1e9,
-                "peak": pk["hbm"], "unit": "GB/s"}
-    roof["frac"] = roof["achieved"] / roof["peak"]
-    roof["traffic"] = traffic
+    peak_kind = "sustained" if ms / 1e3 >= 2.0 else "burst"
+    entries = layer_rooflines(phases, world, pk, peak_kind)
+    roof = dict(next(e for e in entries if e["kernel"] == "gate_up"))
     roof["kernel"] = "grouped gate/up GEMM + fused SiLU-gate on SM pairs (gemm_pair_kernel<2>)"
-    roof["algorithmic"] = {"flop": flops, "bytes": bytes_alg, "ms": gemm_ms,
-                           "peak_src": pk["src"] + " (sustained bf16)"}
+    headline = TOKENS == 8192 and EXPERTS == 64 and world == 1
+    roof["traffic"] = GATE_UP_TRAFFIC["bytes"] if headline else None
+    roof["traffic_src"] = GATE_UP_TRAFFIC["src"] if headline else None
+    roof["timed_region_s"] = ms / 1e3
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -363,30 +446,22 @@ def run_ours(args) -> int:
                               "the neighbouring steps' compute (HostPipeline, depth 2)"},
             "gpu_launches": layer.LAUNCHES_PER_CALL * args.steps,
             "roofline": roof,
+            "kernels_ms": {n: round(v, 5) for n, v in phases.items()},
+            "roofline_kernels": [{k: e[k] for k in ("kernel", "bound", "achieved", "peak",
+                                                   "unit", "frac", "ms")}
+                                 for e in entries],
             "cpu_baseline": cpu,
             "clocks": clocks.summary(wall0, wall1),
         }
+        if parity is not None:
+            line["ep_bitexact"] = parity["bitexact"]
+            line["ep_parity"] = parity
         print(json.dumps(line), flush=True)
     if world > 1:
         layer.close()
         barrier()
         dist.destroy_process_group()
     return 0
-
-
-def profile_traffic():
-    """DRAM bytes per launch of the dominant kernel from the committed ncu
-    summary (a `traffic_bytes_per_launch:` line), or None."""
-    p = ROOT / "profiles" / "moe_pair_gemm_T8192.md"
-    if not p.exists():
-        return None
-    for line in p.read_text().splitlines():
-        if line.strip().startswith("traffic_bytes_per_launch:"):
-            try:
-                return float(line.split(":", 1)[1].strip().split()[0])
-            except ValueError:
-                return None
-    return None
 
 
 # --------------------------------------------------------- reference arm ---

@@ -58,6 +58,12 @@ const char* kvm_sm100_last_error(void);
  * Returns KVM_ERR_TIMEOUT / KVM_ERR_INVALID_ARG when a bit is set. */
 int kvm_sm100_device_status(int* status_out, int clear);
 
+/* The binary architecture the current device runs this library's kernels
+ * from, as cudaFuncAttributes::binaryVersion (major * 10 + minor: 100 for the
+ * sm_100a cubins this library ships). Needs a device. A diagnostic with no
+ * counterpart in the reference. */
+int kvm_sm100_kernel_binary_version(int* version);
+
 /* --------------------------------------------------------------- GEMM --- */
 
 /* D[M,N] = A[M,K] . B  (+ C[M,N] when C != NULL), fp32 accumulation in TMEM.
@@ -113,15 +119,18 @@ int kvm_sm100_moe_router_topk(const void* x, const void* Wr, float* logits,
  * (exclusive prefix of per-expert counts), pos [T*k] (row of pair (t,j) in the
  * permuted order) and src_token [T*k] (token of each permuted row).
  * workspace: kvm_sm100_moe_permute_workspace(T, k, E) bytes of device memory.
- * Bit-exact: no atomics decide any position. */
+ * Bit-exact: no atomics decide any position. A pair whose expert index lies
+ * outside [0, E) gets pos = -1 and joins no group, so expert_offsets[E] is
+ * then below T*k and src_token[expert_offsets[E]..T*k) is not written; the
+ * kernel records it in the device status word (kvm_sm100_device_status). */
 int64_t kvm_sm100_moe_permute_workspace(int T, int k, int E);
 int kvm_sm100_moe_permute(const int32_t* topk_idx, int T, int k, int E,
                           int32_t* expert_offsets, int32_t* pos,
                           int32_t* src_token, void* workspace,
                           kvm_stream_t stream);
 
-/* Allocation-free variant of kvm_sm100_moe_permute, with the same inputs,
- * outputs and results. No counterpart in the reference: it exists for callers
+/* Allocation-free variant of kvm_sm100_moe_permute, with the same inputs and
+ * outputs and no workspace argument. No counterpart in the reference: it exists for callers
  * that cannot allocate GPU memory while they route tokens -- a host program
  * that owns every device buffer through its own pool (an FFI host), or a
  * serving loop that must not call cudaMalloc/cudaFree because they
@@ -133,12 +142,22 @@ int kvm_sm100_moe_permute(const int32_t* topk_idx, int T, int k, int E,
  * done once per device, with that device current); make that first call
  * before any stream capture. All calls on a device share the array, so calls
  * whose kernels overlap on the GPU race and must not be issued. Calls no
- * cudaMalloc, cudaFree or allocating routine. An out-of-range expert index
- * yields pos = -1 for that pair. */
+ * cudaMalloc, cudaFree or allocating routine. Valid indices give outputs
+ * bit-identical to kvm_sm100_moe_permute's. An out-of-range expert index is
+ * handled as there (pos = -1, the pair joins no group), but it is recorded in
+ * a status word of this entry point's own, inside the static array, not in
+ * the device status word: read it with kvm_sm100_moe_permute_noalloc_status. */
 #define KVM_SM100_NOALLOC_PERMUTE_MAX_CELLS 65536
 int kvm_sm100_moe_permute_noalloc(const int32_t* topk_idx, int T, int k, int E,
                                   int32_t* expert_offsets, int32_t* pos,
                                   int32_t* src_token, kvm_stream_t stream);
+/* Synchronise the current device and read (clear != 0: then zero) the status
+ * word of kvm_sm100_moe_permute_noalloc on it; the word is sticky across calls
+ * until cleared. Returns KVM_ERR_INVALID_ARG when a call saw an expert index
+ * outside [0, E). Allocates nothing (two small copies to and from the static
+ * array). No counterpart in the reference: it is the status half of the
+ * allocation-free permute above. */
+int kvm_sm100_moe_permute_noalloc_status(int* status_out, int clear);
 
 /* xp[pos[t*k+j], :] = x[t, :] for every pair: the token scatter of
  * moe_dispatch. x: bf16 [T, H]; xp: bf16 [T*k, H]. */

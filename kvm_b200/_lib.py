@@ -52,6 +52,7 @@ SIGNATURES = {
     "kvm_sm100_version": (_I, []),
     "kvm_sm100_last_error": (C.c_char_p, []),
     "kvm_sm100_device_status": (_I, [C.POINTER(_I), _I]),
+    "kvm_sm100_kernel_binary_version": (_I, [C.POINTER(_I)]),
     "kvm_sm100_gemm_bf16": (_I, [_P, _I64, _P, _I64, _I, _P, _P, _I64, _I, _I, _I, _I, _P]),
     "kvm_sm100_gemm_bf16_silu_gate": (_I, [_P, _I64, _P, _P, _I64, _I, _I, _I, _P]),
     "kvm_sm100_pack_gate_up": (_I, [_P, _P, _P, _I, _I, _I, _I, _P]),
@@ -60,6 +61,7 @@ SIGNATURES = {
     "kvm_sm100_moe_permute_workspace": (_I64, [_I, _I, _I]),
     "kvm_sm100_moe_permute": (_I, [_P, _I, _I, _I, _P, _P, _P, _P, _P]),
     "kvm_sm100_moe_permute_noalloc": (_I, [_P, _I, _I, _I, _P, _P, _P, _P]),
+    "kvm_sm100_moe_permute_noalloc_status": (_I, [C.POINTER(_I), _I]),
     "kvm_sm100_moe_scatter_rows": (_I, [_P, _P, _P, _I, _I, _I, _P]),
     "kvm_sm100_grouped_gemm_bf16": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, _I, _P]),
     "kvm_sm100_moe_combine": (_I, [_P, _P, _P, _P, _I, _I, _I, _P]),

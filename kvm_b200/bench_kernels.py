@@ -23,7 +23,6 @@ quantised per block to amax 448).
 from __future__ import annotations
 
 import json
-from pathlib import Path
 import statistics
 import time
 
@@ -31,23 +30,30 @@ import torch
 
 from . import ops
 
-_PROFILES = Path(__file__).resolve().parents[1] / "profiles"
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one launch of
+# each line's dominant kernel, from the ncu capture summarised in the named
+# file under profiles/ (which gives the command), scaled where that capture
+# ran a smaller case.
+TRAFFIC = {
+    "attn_fwd_B4_L2048_HQ64": (265392384.0, "ncu capture at the bench's own size"),
+    "paged_decode_S16_ctx4096": (1105584128.0, "ncu capture of 16 sequences x4 to the "
+                                               "bench's 64 (each sequence's keys once)"),
+    "fused_elementwise_silu_8192x14336": (677293568.0, "ncu capture at the bench's own size"),
+    "gemm_bf16_1024x1024x1024": (4226304.0, "ncu capture at the bench's own size"),
+    "gated_mlp_T4096_H4096_F14336": (399734272.0, "ncu capture at the bench's own size"),
+    "fp8_gemm_K8192_N28672": (244381440.0, "ncu capture at the bench's own size"),
+}
 
 
 def _traffic(profile: str):
-    """DRAM bytes (read + write) per launch of a line's dominant kernel, from
-    the `traffic_bytes_per_launch:` line of its committed ncu summary, or
-    None when there is none."""
-    p = _PROFILES / f"{profile}.md"
-    if not p.exists():
-        return None
-    for line in p.read_text().splitlines():
-        if line.strip().startswith("traffic_bytes_per_launch:"):
-            try:
-                return float(line.split(":", 1)[1].split()[0])
-            except (ValueError, IndexError):
-                return None
-    return None
+    """DRAM bytes per launch of a line's dominant kernel (TRAFFIC), or None."""
+    t = TRAFFIC.get(profile)
+    return t[0] if t else None
+
+
+def _traffic_src(profile: str):
+    t = TRAFFIC.get(profile)
+    return f"{t[1]}: profiles/{profile}.md" if t else None
 
 
 def _time(fn, steps, warmup, flush=None):
@@ -233,6 +239,7 @@ def run_attn(args, peaks, ClockSampler, dev, g) -> int:
           roofline={"bound": "tensor", "achieved": tf, "peak": peaks["bf16"],
                     "unit": "TFLOP/s", "frac": tf / peaks["bf16"],
                     "traffic": _traffic("attn_fwd_B4_L2048_HQ64"),
+                    "traffic_src": _traffic_src("attn_fwd_B4_L2048_HQ64"),
                     "kernel": "attn_fwd_kernel"},
           gpu_launches=steps)
     return 0
@@ -288,6 +295,7 @@ def run_decode(args, peaks, ClockSampler, dev, g) -> int:
           roofline={"bound": "hbm", "achieved": gbs, "peak": peaks["hbm"], "unit": "GB/s",
                     "frac": gbs / peaks["hbm"],
                     "traffic": _traffic("paged_decode_S16_ctx4096") if S == 64 else None,
+                    "traffic_src": _traffic_src("paged_decode_S16_ctx4096") if S == 64 else None,
                     "kernel": "decode_attn_kernel + combine + kvcache.write"},
           gpu_launches=3 * steps)
     return 0
@@ -352,6 +360,7 @@ def run_ew(args, peaks, ClockSampler, dev, g) -> int:
           roofline={"bound": "hbm", "achieved": gbs, "peak": peaks["hbm"], "unit": "GB/s",
                     "frac": gbs / peaks["hbm"],
                     "traffic": _traffic("fused_elementwise_silu_8192x14336"),
+                    "traffic_src": _traffic_src("fused_elementwise_silu_8192x14336"),
                     "kernel": "kvm_ew (generated)"},
           gpu_launches=steps)
     return 0
@@ -384,7 +393,8 @@ def run(args, peaks, ClockSampler) -> int:
                       "l2": "flushed before each launch (256 MB read)"},
               roofline={"bound": "tensor", "achieved": tf, "peak": peaks["bf16"],
                         "unit": "TFLOP/s", "frac": tf / peaks["bf16"],
-                        "traffic": _traffic("gemm_bf16_1024x1024x1024")},
+                        "traffic": _traffic("gemm_bf16_1024x1024x1024"),
+                        "traffic_src": _traffic_src("gemm_bf16_1024x1024x1024")},
               gpu_launches=steps)
         return 0
     if args.workload == "decode":
@@ -428,6 +438,7 @@ def run(args, peaks, ClockSampler) -> int:
               roofline={"bound": "tensor", "achieved": gu_tf, "peak": peaks["bf16_sustained"],
                         "unit": "TFLOP/s", "frac": gu_tf / peaks["bf16_sustained"],
                         "traffic": _traffic("gated_mlp_T4096_H4096_F14336"),
+                    "traffic_src": _traffic_src("gated_mlp_T4096_H4096_F14336"),
                         "kernel": "gate/up GEMM + fused SiLU-gate",
                         "ms": t_gu},
               gpu_launches=3 * steps)
@@ -472,6 +483,7 @@ def run(args, peaks, ClockSampler) -> int:
                   "fp8_peak_tflops": f"{fp8_peak:.0f} (2 x measured bf16)"},
           roofline={"bound": "hbm", "achieved": r16["gbs"], "peak": peaks["hbm"],
                     "unit": "GB/s", "frac": r16["gbs"] / peaks["hbm"],
-                    "traffic": _traffic("fp8_gemm_K8192_N28672")},
+                    "traffic": _traffic("fp8_gemm_K8192_N28672"),
+                        "traffic_src": _traffic_src("fp8_gemm_K8192_N28672")},
           gpu_launches=3 * steps)
     return 0

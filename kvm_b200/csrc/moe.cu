@@ -448,7 +448,9 @@ namespace kvm {
 namespace {
 
 constexpr int kNoAllocMaxCells = KVM_SM100_NOALLOC_PERMUTE_MAX_CELLS;
-// [0, cells): counts; [cells, 2*cells): bases; then one status word.
+// [0, cells): counts; [cells, 2*cells): bases; then the status word of this
+// entry point (bit kDevBadInput: a pair named an expert outside [0, E)),
+// read and cleared by kvm_sm100_moe_permute_noalloc_status.
 static __device__ __align__(256) int g_permute_scratch[2 * kNoAllocMaxCells + 64];
 
 constexpr int kNoAllocMaxDevices = 64;
@@ -477,6 +479,25 @@ int noalloc_scratch(int** out) {
 
 }  // namespace
 }  // namespace kvm
+
+extern "C" int kvm_sm100_moe_permute_noalloc_status(int* status_out, int clear) {
+  int* scratch = nullptr;
+  if (int rc = noalloc_scratch(&scratch); rc != KVM_OK) return rc;
+  int* word = scratch + 2 * kNoAllocMaxCells;
+  int v = 0;
+  // Plain copies into and out of the static array: nothing is allocated.
+  KVM_CUDA_TRY(cudaDeviceSynchronize());
+  KVM_CUDA_TRY(cudaMemcpy(&v, word, sizeof(int), cudaMemcpyDeviceToHost));
+  if (clear) {
+    const int zero = 0;
+    KVM_CUDA_TRY(cudaMemcpy(word, &zero, sizeof(int), cudaMemcpyHostToDevice));
+  }
+  if (status_out) *status_out = v;
+  if (v & kDevBadInput)
+    return fail(KVM_ERR_INVALID_ARG,
+                "moe_permute_noalloc: an expert index was outside [0, E)");
+  return KVM_OK;
+}
 
 extern "C" int kvm_sm100_moe_permute_noalloc(const int32_t* topk_idx, int T,
                                              int k, int E,

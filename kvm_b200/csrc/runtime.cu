@@ -111,9 +111,25 @@ int encode_tmap_2d(CUtensorMap* map, const void* base, uint64_t inner,
 
 }  // namespace kvm
 
+namespace kvm {
+namespace {
+// An empty kernel whose attributes stand for every kernel of this library
+// (all translation units are compiled with the same -gencode).
+__global__ void binary_version_probe_kernel() {}
+}  // namespace
+}  // namespace kvm
+
 extern "C" {
 
 const char* kvm_sm100_last_error(void) { return kvm::t_last_error.c_str(); }
+
+int kvm_sm100_kernel_binary_version(int* version) {
+  if (!version) return kvm::fail(KVM_ERR_INVALID_ARG, "kernel_binary_version: NULL");
+  cudaFuncAttributes a;
+  KVM_CUDA_TRY(cudaFuncGetAttributes(&a, kvm::binary_version_probe_kernel));
+  *version = a.binaryVersion;
+  return KVM_OK;
+}
 
 int kvm_sm100_version(void) { return KVM_SM100_ABI_VERSION; }
 

@@ -196,7 +196,7 @@ class ExpertParallelMoENccl:
     def _g(self, r: int) -> int:
         return r if self.group is None else dist.get_global_rank(self.group, r)
 
-    def __call__(self, x, probe=None):
+    def __call__(self, x):
         T = x.shape[0]
         c = self.compute
         xp, offsets = c.dispatch_local(x)
@@ -208,11 +208,7 @@ class ExpertParallelMoENccl:
                          both[self.E + 1:].tolist())
         self.last_plan = plan
         self._exchange(xp, c.recv, plan.send, plan.recv)
-        if probe is not None:
-            probe[0].record()
         y = c.experts(plan.recv_rows, plan.local_offsets)
-        if probe is not None:
-            probe[1].record()
         # reverse: what was received from (peer, row) goes back to (peer, row)
         self._exchange(y, c.yback, plan.recv, plan.send)
         return c.combine_local(T)
@@ -309,9 +305,14 @@ class ExpertParallelMoE:
         if world > 1:
             dist.barrier(group=group)
 
+    # phase marks of a call (kvm_b200.timing.PhaseProbe): one per launch
+    PHASES = ["start", "router", "permute", "ep_counts", "ep_dispatch", "ep_wait_data",
+              "gate_up", "down", "ep_signal", "ep_wait_outputs", "ep_combine"]
+
     def __call__(self, x, probe=None, out=None):
         from ._lib import call
         from .moe import _out_buffer
+        mark = probe.mark if probe is not None else (lambda name: None)
         T, H = x.shape
         if H != self.H or T > self.max_tokens or T <= 0:
             raise ValueError(f"x must be [T <= {self.max_tokens}, {self.H}]")
@@ -322,31 +323,38 @@ class ExpertParallelMoE:
         ep, pr = self.epoch, self._peers_ref
         st = torch.cuda.current_stream().cuda_stream
         E, k, F = self.E, self.k, self.F
+        mark("start")
         call("kvm_sm100_moe_router_topk", x.data_ptr(), self.w_router.data_ptr(),
              self.logits.data_ptr(), self.idx.data_ptr(), self.topw.data_ptr(),
              T, H, E, k, st)
+        mark("router")
         call("kvm_sm100_moe_permute", self.idx.data_ptr(), T, k, E, self.offsets.data_ptr(),
              self.pos.data_ptr(), self.src.data_ptr(), self.ws.data_ptr(), st)
+        mark("permute")
         call("kvm_sm100_ep_counts", pr, self.offsets.data_ptr(), self.send_base.data_ptr(),
              self.loc_off.data_ptr(), ep, st)
+        mark("ep_counts")
         call("kvm_sm100_ep_dispatch", pr, x.data_ptr(), self.idx.data_ptr(),
              self.pos.data_ptr(), self.offsets.data_ptr(), self.send_base.data_ptr(), T,
              self.cap, self.done.data_ptr(), ep, st)
+        mark("ep_dispatch")
         call("kvm_sm100_ep_wait", pr, 1, ep, st)
-        if probe is not None:
-            probe[0].record()
+        mark("ep_wait_data")
         recv, y = self._own["recv"], self._own["y"]
         call("kvm_sm100_grouped_gemm_bf16", recv, self.w13.data_ptr(), self.h.data_ptr(),
              self.loc_off.data_ptr(), self.epr, self.cap, 2 * F, H, 2, st)
-        if probe is not None:
-            probe[1].record()
+        mark("gate_up")
         call("kvm_sm100_grouped_gemm_bf16", self.h.data_ptr(), self.w2.data_ptr(), y,
              self.loc_off.data_ptr(), self.epr, self.cap, H, F, 0, st)
+        mark("down")
         call("kvm_sm100_ep_signal", pr, 2, ep, st)
+        mark("ep_signal")
         call("kvm_sm100_ep_wait", pr, 2, ep, st)
+        mark("ep_wait_outputs")
         call("kvm_sm100_ep_combine", pr, self.idx.data_ptr(), self.pos.data_ptr(),
              self.offsets.data_ptr(), self.send_base.data_ptr(), self.topw.data_ptr(),
              dst.data_ptr(), T, self.cap, st)
+        mark("ep_combine")
         return dst[:T]
 
     def close(self):

@@ -101,12 +101,16 @@ class MoELayer:
         n = self._n * self.k
         return ops.Dispatch(self.offsets, self.pos[:n], self.src_token[:n])
 
+    # phase marks of a call (kvm_b200.timing.PhaseProbe): one per launch
+    PHASES = ["start", "router", "permute", "scatter", "gate_up", "down", "combine"]
+
     def __call__(self, x: torch.Tensor, probe=None, out: torch.Tensor | None = None
                  ) -> torch.Tensor:
-        """Run the layer on x [T, H]; `probe` = (start, end) CUDA events to
-        record around the gate/up grouped GEMM (for per-kernel timing); `out`
-        (contiguous bf16 [>= T, H]) receives the result instead of the layer's
-        own buffer."""
+        """Run the layer on x [T, H]; `probe` (a kvm_b200.timing.PhaseProbe
+        over PHASES) records a CUDA event before the first launch and after
+        each launch, for per-kernel timing; `out` (contiguous bf16 [>= T, H])
+        receives the result instead of the layer's own buffer."""
+        mark = probe.mark if probe is not None else (lambda name: None)
         T, H = x.shape
         if H != self.H or T > self.max_tokens or T <= 0:
             raise ValueError(f"x must be [T<= {self.max_tokens}, {self.H}]")
@@ -115,25 +119,28 @@ class MoELayer:
         self._n = T
         st = torch.cuda.current_stream().cuda_stream
         E, F, k = self.E, self.F, self.k
+        dst = _out_buffer(out, self.out, T, H)
+        mark("start")
         call("kvm_sm100_moe_router_topk", x.data_ptr(), self.w_router.data_ptr(),
              self.logits.data_ptr(), self.topk_idx.data_ptr(), self.topk_w.data_ptr(),
              T, H, E, k, st)
+        mark("router")
         call("kvm_sm100_moe_permute", self.topk_idx.data_ptr(), T, k, E,
              self.offsets.data_ptr(), self.pos.data_ptr(), self.src_token.data_ptr(),
              self.workspace.data_ptr(), st)
+        mark("permute")
         call("kvm_sm100_moe_scatter_rows", x.data_ptr(), self.pos.data_ptr(),
              self.xp.data_ptr(), T, k, H, st)
-        if probe is not None:
-            probe[0].record()
+        mark("scatter")
         call("kvm_sm100_grouped_gemm_bf16", self.xp.data_ptr(), self.w13.data_ptr(),
              self.h.data_ptr(), self.offsets.data_ptr(), E, T * k, 2 * F, H, 2, st)
-        if probe is not None:
-            probe[1].record()
+        mark("gate_up")
         call("kvm_sm100_grouped_gemm_bf16", self.h.data_ptr(), self.w2.data_ptr(),
              self.y.data_ptr(), self.offsets.data_ptr(), E, T * k, H, F, 0, st)
-        dst = _out_buffer(out, self.out, T, H)
+        mark("down")
         call("kvm_sm100_moe_combine", self.y.data_ptr(), self.pos.data_ptr(),
              self.topk_w.data_ptr(), dst.data_ptr(), T, k, H, st)
+        mark("combine")
         return dst[:T]
 
     @property

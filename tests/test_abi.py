@@ -1,7 +1,6 @@
 """The C-ABI library loads, exports every symbol include/kvm_sm100.h declares,
 and rejects bad arguments before touching a GPU (runs on CPU)."""
 import ctypes as C
-import subprocess
 from pathlib import Path
 
 import pytest
@@ -76,12 +75,20 @@ def test_product_code_never_imports_the_oracle():
 
 
 def test_kernels_built_for_sm100a_only():
-    out = subprocess.run(["cuobjdump", "--list-elf", str(_lib.LIB_PATH)],
-                         capture_output=True, text=True)
-    if out.returncode != 0:
-        pytest.skip("cuobjdump unavailable")
-    archs = {line.split(".")[-2] for line in out.stdout.split() if line.endswith(".cubin")}
-    assert archs == {"sm_100a"}, archs
+    """Every translation unit and the link step get exactly one -gencode,
+    sm_100a cubins with no PTX to JIT elsewhere (the GPU test below reads the
+    binary version the device actually runs)."""
+    from kvm_b200 import build as kbuild
+    assert kbuild.ARCH == ["-gencode", "arch=compute_100a,code=sm_100a"]
+    flags = " ".join(kbuild.NVCC_FLAGS)
+    assert "-gencode" not in flags and "-arch" not in flags
+
+
+@pytest.mark.gpu
+def test_device_runs_the_sm100_cubins(cuda):
+    v = C.c_int(0)
+    _lib.call("kvm_sm100_kernel_binary_version", C.byref(v))
+    assert v.value == 100
 
 
 def test_fp8_workspace_plan():
