@@ -106,7 +106,9 @@ int kvm_sm100_transpose_bf16(const void* in, void* out, int G, int R, int C,
  * (Wr stored [E, H]); probabilities p = softmax(logits) in fp32; topk_idx
  * [T,k] are the k largest logits per token (ties: lower expert index first,
  * descending order), topk_w [T,k] their probabilities (no renormalisation).
- * 1 <= E <= 64 in this build; 1 <= k <= min(8, E).
+ * 1 <= E <= 256 in this build (E > 256: KVM_ERR_UNSUPPORTED); 1 <= k <= min(8, E).
+ * A token's logits are the same bits in any batch: K is accumulated in fixed
+ * chunks added in a fixed order, whichever tile or CTA computes the row.
  * Replaces the routing half of kernel.comm.moe_dispatch
  * (src/ir/dialect/kernel/dialect.cpp:65, passed through to
  * task.comm.moe_dispatch by src/device/device.cpp:143-147). */

@@ -1,12 +1,14 @@
 // Host launchers of the bf16 tcgen05 GEMM: dense GEMM (kernel.matmul /
 // kernel.gemm), the fused SiLU-gate GEMM, the grouped expert GEMM and the
 // router GEMM with fused softmax/top-k.
+#include <algorithm>
 #include <cstdlib>
 #include <cstring>
 #include <mutex>
 
 #include "gemm_bf16.cuh"
 #include "gemm_pair.cuh"
+#include "router.cuh"
 #include "runtime.h"
 
 namespace kvm {
@@ -316,12 +318,30 @@ extern "C" int kvm_sm100_grouped_gemm_bf16(const void* A, const void* B,
                       static_cast<cudaStream_t>(stream));
 }
 
+namespace kvm {
+namespace {
+
+template <int BN>
+int launch_router(const CUtensorMap& tx, const CUtensorMap& tw, const RouterParams& p,
+                  int grid, cudaStream_t st) {
+  auto kern = router_topk_kernel<BN>;
+  constexpr size_t smem = RouterCfg<BN>::kSmem;
+  KVM_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    int(smem)));
+  kern<<<grid, kRouterThreads, smem, st>>>(tx, tw, p);
+  KVM_CUDA_TRY(cudaGetLastError());
+  return KVM_OK;
+}
+
+}  // namespace
+}  // namespace kvm
+
 extern "C" int kvm_sm100_moe_router_topk(const void* x, const void* Wr,
                                          float* logits, int32_t* topk_idx,
                                          float* topk_w, int T, int H, int E,
                                          int k, kvm_stream_t stream) {
-  if (E < 1 || E > 64)
-    return fail(KVM_ERR_UNSUPPORTED, "router: this build supports 1 <= E <= 64");
+  if (E < 1 || E > 256)
+    return fail(KVM_ERR_UNSUPPORTED, "router: this build supports 1 <= E <= 256");
   if (T <= 0 || H <= 0 || H % 8 != 0 || k < 1 || k > 8 || k > E)
     return fail(KVM_ERR_INVALID_ARG,
                 "router: need T > 0, H % 8 == 0 and 1 <= k <= min(8, E)");
@@ -332,26 +352,32 @@ extern "C" int kvm_sm100_moe_router_topk(const void* x, const void* Wr,
     return fail(KVM_ERR_INVALID_ARG, "router: outputs are NULL");
   const DeviceInfo* dev = device_info();
   if (!dev) return KVM_ERR_CUDA;
-  GemmParams p{};
-  p.M = T; p.N = E; p.K = H;
-  p.num_groups = 1; p.offsets = nullptr; p.b_group_rows = 0;
-  p.D = logits; p.ldd = E;
-  p.logits = logits; p.topk_idx = topk_idx; p.topk_w = topk_w; p.top_k = k;
+  const int BN = E <= 64 ? 64 : E <= 128 ? 128 : 256;
+  RouterParams p{};
+  p.T = T; p.E = E; p.K = H; p.top_k = k;
+  p.logits = logits; p.topk_idx = topk_idx; p.topk_w = topk_w;
   p.status = dev->status;
   // Rows per tile: enough tiles to give every SM one (8192 tokens on 148
   // SMs: 147 tiles of 56 rows), at least 32 rows and at most 128.
   int tr = (cdiv(T, dev->sm_count) + 7) & ~7;
-  tr = tr < 32 ? 32 : tr > kGemmBM ? kGemmBM : tr;
+  tr = tr < 32 ? 32 : tr > 128 ? 128 : tr;
   p.tile_rows = tr;
+  // K chunks: as many accumulators as TMEM holds (512 columns), none empty.
+  const int kb_total = cdiv(H, kRouterBK);
+  int nch = std::min(512 / BN, kb_total);
+  const int kpc = cdiv(kb_total, nch);
+  p.nch = cdiv(kb_total, kpc);
   const int tiles = cdiv(T, tr);
   const int grid = tiles < dev->sm_count ? tiles : dev->sm_count;
-  CUtensorMap ta, tb;
-  KVM_TRY(encode_tmap_2d(&ta, x, H, T, (uint64_t)H * 2, kGemmBK, tr,
+  CUtensorMap tx, tw;
+  KVM_TRY(encode_tmap_2d(&tx, x, H, T, (uint64_t)H * 2, kRouterBK, tr,
                          CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
                          CU_TENSOR_MAP_SWIZZLE_128B));
-  KVM_TRY(encode_tmap_2d(&tb, Wr, H, E, (uint64_t)H * 2, kGemmBK, 64,  // rows >= E read 0
+  KVM_TRY(encode_tmap_2d(&tw, Wr, H, E, (uint64_t)H * 2, kRouterBK, BN,  // rows >= E read 0
                          CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
                          CU_TENSOR_MAP_SWIZZLE_128B));
-  return launch<64, 8, false, kEpiRouter>(ta, tb, tb, p, grid,
-                                          static_cast<cudaStream_t>(stream));
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (BN == 64) return launch_router<64>(tx, tw, p, grid, st);
+  if (BN == 128) return launch_router<128>(tx, tw, p, grid, st);
+  return launch_router<256>(tx, tw, p, grid, st);
 }

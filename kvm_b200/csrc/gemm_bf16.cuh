@@ -25,7 +25,6 @@ enum GemmEpilogue : int {
   kEpiF32 = 1,     // D = acc [+ C] (fp32)
   kEpiSilu = 2,    // per 128 tile cols: 64 gate, then the 64 up of the same
                    // f (pack_gate_up layout) -> bf16 SiLU(g)*u
-  kEpiRouter = 3,  // BN = 64 >= E: logits + softmax + top-k per row
 };
 
 constexpr int kGemmBM = 128;
@@ -44,15 +43,9 @@ struct GemmParams {
   long long ldd;         // elements
   const void* C;         // optional addend (same dtype as D), row stride ldc
   long long ldc;
-  float* logits;         // router epilogue outputs
-  int* topk_idx;
-  float* topk_w;
-  int top_k;
   int* status;           // device status word
   int split_tiles;       // the last split_tiles tiles run as two half-width
                          // items each (BN >= 128; 0: none)
-  int tile_rows;         // router only: rows per tile, a multiple of 8 in
-                         // [8, 128] (0: 128); A's tensor map box has as many
 };
 
 // Where one output tile's operands and results live.
@@ -174,11 +167,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   constexpr uint32_t kIdesc = idesc_bf16(BM, BN, 0, B_MN ? 1 : 0);
   constexpr uint32_t kIdescHalf = idesc_bf16(BM, BN / 2, 0, B_MN ? 1 : 0);
   constexpr bool kCanSplit = BN >= 128;
-  // Rows per tile. The router takes fewer than 128 so that its tiles fill the
-  // SMs (it streams x once, and a CTA's share of the bytes sets its time);
-  // the MMA stays M = 128 and TMEM lanes at or past TR, whose A rows in
-  // shared memory the TMA never writes, are not read back.
-  const int TR = (EPI == kEpiRouter && p.tile_rows > 0) ? p.tile_rows : BM;
+  constexpr int TR = BM;  // rows per tile
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
@@ -381,7 +370,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
                              acc * BN;
       const int row = row0 + r_in_tile;
-      const bool row_ok = row < row_end && r_in_tile < TR;
+      const bool row_ok = row < row_end;
 
       if constexpr (EPI == kEpiBf16 || EPI == kEpiF32) {
         constexpr bool F32 = EPI == kEpiF32;
@@ -422,56 +411,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             char* dst = static_cast<char*>(p.D) +
                         (static_cast<long long>(row) * p.ldd + col) * 2;
             store_row32<false>(dst, nullptr, v, min(32, p.N / 2 - col));
-          }
-        }
-      } else {  // kEpiRouter: BN == 64 tile columns, the first p.N are experts
-        uint32_t r0[32], r1[32];
-        tmem_ld32(t_row, r0);
-        tmem_ld32(t_row + 32, r1);
-        tmem_wait_ld();
-        if (row_ok) {
-          const int E = p.N;
-          float l[64];
-#pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            l[i] = __uint_as_float(r0[i]);
-            l[32 + i] = __uint_as_float(r1[i]);
-          }
-          float* lrow = p.logits + static_cast<long long>(row) * E;
-          if (E == 64) {
-#pragma unroll
-            for (int i = 0; i < 16; ++i)
-              reinterpret_cast<float4*>(lrow)[i] =
-                  make_float4(l[4 * i], l[4 * i + 1], l[4 * i + 2], l[4 * i + 3]);
-          } else {
-#pragma unroll
-            for (int i = 0; i < 64; ++i)
-              if (i < E) lrow[i] = l[i];
-          }
-          float mx = l[0];
-#pragma unroll
-          for (int i = 1; i < 64; ++i)
-            if (i < E) mx = fmaxf(mx, l[i]);
-          float sum = 0.f;
-#pragma unroll
-          for (int i = 0; i < 64; ++i)
-            if (i < E) sum += expf(l[i] - mx);
-          uint64_t taken = 0;
-          for (int j = 0; j < p.top_k; ++j) {
-            float best = -INFINITY;
-            int bi = -1;
-#pragma unroll
-            for (int i = 0; i < 64; ++i) {
-              const bool free_i = i < E && ((taken >> i) & 1ull) == 0;
-              if (free_i && (bi < 0 || l[i] > best)) {
-                best = l[i];
-                bi = i;
-              }
-            }
-            taken |= 1ull << bi;
-            p.topk_idx[static_cast<long long>(row) * p.top_k + j] = bi;
-            p.topk_w[static_cast<long long>(row) * p.top_k + j] =
-                expf(best - mx) / sum;
           }
         }
       }

@@ -6,7 +6,9 @@ target.
 
 The front end (parser, serializer, graph, kernel/task/tile dialects, the
 kernel->task transform) is compiled from the reference's own sources where
-they lie (default: $KVM_REFERENCE_DIR or /root/reference); nothing is copied.
+they lie (--ref DIR, else $KVM_REFERENCE_DIR; there is no default); nothing is
+copied. The tree used is recorded in kvm_b200/_build/host/reference_dir.txt
+so that later steps (the CMake build check) find the same one.
 Two build-time shims are needed because of this machine's toolchain:
   * glog is not installed: kvm_b200/host/shim/glog/logging.h supplies CHECK;
   * GCC rejects `struct ::kvm::ir::MarkMember<...>` (a global qualifier before
@@ -58,8 +60,20 @@ BAD = b"struct ::kvm::ir::MarkMember"
 GOOD = b"struct kvm::ir::MarkMember"
 
 
-def ref_dir(arg: str | None) -> Path:
-    return Path(arg or os.environ.get("KVM_REFERENCE_DIR", "/root/reference"))
+def ref_dir(arg: str | None) -> Path | None:
+    """The reference tree: the argument, else $KVM_REFERENCE_DIR, else None."""
+    d = arg or os.environ.get("KVM_REFERENCE_DIR")
+    return Path(d) if d else None
+
+
+def recorded_ref_dir() -> Path | None:
+    """The reference tree the last successful build used, if any."""
+    f = OUT / "reference_dir.txt"
+    if f.exists():
+        d = Path(f.read_text().strip())
+        if (d / "src" / "ir" / "graph.cpp").exists():
+            return d
+    return None
 
 
 def includes(ref: Path) -> list[str]:
@@ -112,9 +126,10 @@ def cuda_libdirs() -> list[str]:
 
 def build(ref_arg: str | None = None, verbose: bool = False) -> bool:
     ref = ref_dir(ref_arg)
-    if not (ref / "src" / "ir" / "graph.cpp").exists():
+    if ref is None or not (ref / "src" / "ir" / "graph.cpp").exists():
         if verbose:
-            print(f"host build skipped: no reference sources at {ref}")
+            print("host build skipped: no reference sources "
+                  f"({'set KVM_REFERENCE_DIR or pass --ref' if ref is None else ref})")
         return False
     OUT.mkdir(parents=True, exist_ok=True)
     jobs = [(ref / s, OUT / (s.replace("/", "_")[:-4] + ".o")) for s in FRONTEND]
@@ -135,6 +150,7 @@ def build(ref_arg: str | None = None, verbose: bool = False) -> bool:
         raise RuntimeError("build libkvm_sm100.so first (python -m kvm_b200.build)")
     link(OUT / "kvm_run", [OUT / "kvm_kvm_run.o", OUT / "kvm_executor.o",
                            OUT / "kvm_task_to_tile.o", device, *front], extra)
+    (OUT / "reference_dir.txt").write_text(str(ref.resolve()) + "\n")
     if verbose:
         print(f"built host binaries in {OUT}")
     return True

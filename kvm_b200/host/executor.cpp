@@ -478,7 +478,7 @@ void Executor::Fuse() {
     if (src.kind != Slot::kMma || src.args.size() != 2) continue;
     const Buffer& b = slot(BaseGlobal(src.args[1])).buf;
     const Buffer& a = slot(BaseGlobal(src.args[0])).buf;
-    if (b.shape.size() != 2 || b.shape[1] > 64 || b.dtype != Dtype::kBf16 ||
+    if (b.shape.size() != 2 || b.shape[1] > 256 || b.dtype != Dtype::kBf16 ||
         a.dtype != Dtype::kBf16 || slot(dst).buf.dtype != Dtype::kF32 ||
         a.shape.size() != 2 || a.shape[1] % 8 != 0)
       continue;

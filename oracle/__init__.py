@@ -257,6 +257,28 @@ def moe_combine(y: np.ndarray, pos: np.ndarray, w: np.ndarray) -> np.ndarray:
     return out
 
 
+def moe_layer_given_routing(x, w13, w2, idx, tw):
+    """The MoE layer after routing, for a given top-k (idx [T,k] int32, tw
+    [T,k] fp32): permute, scatter, grouped SiLU-gate GEMM, grouped down GEMM,
+    combine -- the same steps orc_moe_layer takes after its own top-k."""
+    E = w13.shape[0]
+    k = idx.shape[1]
+    off, pos, _ = moe_permute(idx, E)
+    xp = moe_scatter_rows(x, pos, k)
+    h = grouped_gemm(xp, w13, off, silu_gate=True)
+    y = grouped_gemm(h, w2, off)
+    return moe_combine(y, pos, tw)
+
+
+def topk_gap(logits: np.ndarray, k: int) -> np.ndarray:
+    """Per row, the fp32 gap between the k-th and (k+1)-th largest logit: a
+    row whose top-k can flip under fp32 reassociation has a gap near 0."""
+    s = -np.sort(-np.asarray(logits, dtype=np.float32), axis=1)
+    if s.shape[1] <= k:
+        return np.full(s.shape[0], np.inf, dtype=np.float32)
+    return s[:, k - 1] - s[:, k]
+
+
 def moe_layer(x, w_router, w13, w2, k: int):
     """Whole MoE layer; returns (out, logits, topk_idx, topk_w)."""
     x, wr = _c(x, np.uint16), _c(w_router, np.uint16)

@@ -32,8 +32,12 @@ def test_invalid_shapes_rejected_without_gpu():
     rc = L.kvm_sm100_gemm_bf16(null, 0, null, 0, 0, null, null, 0, 0, 0, 0, 0, null)
     assert rc == _lib.KVM_ERR_INVALID_ARG
     assert b"positive" in L.kvm_sm100_last_error()
-    rc = L.kvm_sm100_moe_router_topk(null, null, null, null, null, 16, 64, 96, 2, null)
+    # E = 300 experts: beyond the router's 256 (the permute takes up to 1024)
+    rc = L.kvm_sm100_moe_router_topk(null, null, null, null, null, 16, 64, 300, 2, null)
     assert rc == _lib.KVM_ERR_UNSUPPORTED
+    # E = 96 passes the expert bound and stops at the NULL pointers
+    rc = L.kvm_sm100_moe_router_topk(null, null, null, null, null, 16, 64, 96, 2, null)
+    assert rc == _lib.KVM_ERR_INVALID_ARG
     rc = L.kvm_sm100_moe_permute(null, 4, 9, 64, null, null, null, null, null)
     assert rc == _lib.KVM_ERR_INVALID_ARG
     rc = L.kvm_sm100_rmsnorm_bf16(null, null, null, 4, 12, C.c_float(1e-5), null)

@@ -205,3 +205,22 @@ def test_paged_kv_oracle_matches_dense_attention():
         # layer 0 untouched
         other = oracle.kvcache_read(pool, st, bs, 0, W, [0, L], bt, [0, 5])[0]
         assert not other.any()
+
+
+def test_moe_layer_given_routing_matches_the_whole_layer():
+    """The composed post-routing oracle (permute, scatter, grouped GEMMs,
+    combine) reproduces orc_moe_layer bit for bit when given its routing, and
+    the router logits the layer tests compute separately are the layer's."""
+    rng = np.random.default_rng(5)
+    T, H, E, F, k = 96, 64, 8, 128, 2
+    x = oracle.normal_bf16(rng, (T, H))
+    wr = oracle.normal_bf16(rng, (E, H), 0.02)
+    w13 = oracle.normal_bf16(rng, (E, 2 * F, H), 0.02)
+    w2 = oracle.normal_bf16(rng, (E, H, F), 0.02)
+    out, logits, idx, tw = oracle.moe_layer(x, wr, w13, w2, k)
+    assert np.array_equal(oracle.moe_layer_given_routing(x, w13, w2, idx, tw), out)
+    lg = oracle.gemm(x, wr, b_layout="nk", out_f32=True)
+    assert np.array_equal(lg.view(np.uint32), logits.view(np.uint32))
+    gaps = oracle.topk_gap(logits, k)
+    s = np.sort(logits, axis=1)
+    assert np.allclose(gaps, s[:, -k] - s[:, -k - 1])
