@@ -65,6 +65,9 @@ def parse_args(argv=None):
                          "decode: paged decode attention, --seqs sequences x 4096 keys; "
                          "ew: generated fused elementwise programs (SiLU-gate, RMSNorm "
                          "scaling) vs the interpreter")
+    ap.add_argument("--ep-exchange", choices=["overlap", "serial"], default="overlap",
+                    help="N > 1: the all-to-all fused into the grouped GEMMs (default) "
+                         "or the serial exchange kernels (for comparison)")
     ap.add_argument("--seqs", type=int, default=64,
                     help="decode workload: sequences per step (64; smaller values are "
                          "profiling cases)")
@@ -269,6 +272,9 @@ def layer_rooflines(phases: dict, world: int, pk: dict, peak_kind: str) -> list:
         "ep_dispatch": (None, T * H * 2 + R * H * 2),
         "ep_combine": (None, R * H * 2 + T * H * 2),
     }
+    # the overlapped exchange runs the all-to-all inside the grouped GEMMs
+    work["ep_dispatch_gate_up"] = work["gate_up"]
+    work["ep_down_push"] = work["down"]
     out = []
     for name, (flop, nbytes) in work.items():
         if name in phases and phases[name] > 0:
@@ -331,7 +337,8 @@ def run_ours(args) -> int:
     if world > 1:
         from kvm_b200.ep import ExpertParallelMoE
         layer = ExpertParallelMoE(wr, w13, w2, top_k=TOP_K, max_tokens=TOKENS,
-                                  rank=rank, world=world)
+                                  rank=rank, world=world,
+                                  overlap=args.ep_exchange == "overlap")
         if rank != 0:      # rank 0 keeps all experts for the parity check
             w13 = w2 = None
     else:
@@ -418,8 +425,11 @@ def run_ours(args) -> int:
     pk = peaks()
     peak_kind = "sustained" if ms / 1e3 >= 2.0 else "burst"
     entries = layer_rooflines(phases, world, pk, peak_kind)
-    roof = dict(next(e for e in entries if e["kernel"] == "gate_up"))
-    roof["kernel"] = "grouped gate/up GEMM + fused SiLU-gate on SM pairs (gemm_pair_kernel<2>)"
+    roof = dict(next(e for e in entries if e["kernel"] in ("gate_up", "ep_dispatch_gate_up")))
+    roof["kernel"] = ("grouped gate/up GEMM + fused SiLU-gate on SM pairs (gemm_pair_kernel<2>)"
+                      if roof["kernel"] == "gate_up" else
+                      "dispatch all-to-all fused with the grouped gate/up GEMM + SiLU-gate "
+                      "on SM pairs (gemm_pair_kernel<2, 1>)")
     headline = TOKENS == 8192 and EXPERTS == 64 and world == 1
     roof["traffic"] = GATE_UP_TRAFFIC["bytes"] if headline else None
     roof["traffic_src"] = GATE_UP_TRAFFIC["src"] if headline else None
@@ -438,6 +448,7 @@ def run_ours(args) -> int:
             "config": {"workload": config_name(), "tokens_per_rank": TOKENS, "hidden": HIDDEN,
                        "experts": EXPERTS, "ffn": FFN, "top_k": TOP_K,
                        "parallelism": f"ep{world}" if world > 1 else "single",
+                       **({"ep_exchange": args.ep_exchange} if world > 1 else {}),
                        "l2": "inputs larger than L2 (2.2 GB weights per step)"},
             "e2e": {"value": e2e_value, "unit": UNIT,
                     "h2d_bytes_per_step": TOKENS * HIDDEN * 2,

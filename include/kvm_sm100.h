@@ -107,8 +107,8 @@ int kvm_sm100_transpose_bf16(const void* in, void* out, int G, int R, int C,
  * [T,k] are the k largest logits per token (ties: lower expert index first,
  * descending order), topk_w [T,k] their probabilities (no renormalisation).
  * 1 <= E <= 256 in this build (E > 256: KVM_ERR_UNSUPPORTED); 1 <= k <= min(8, E).
- * A token's logits are the same bits in any batch: K is accumulated in fixed
- * chunks added in a fixed order, whichever tile or CTA computes the row.
+ * A token's logits are the same bits in any batch: one accumulator, K always
+ * in the same order, whichever tile or CTA computes the row.
  * Replaces the routing half of kernel.comm.moe_dispatch
  * (src/ir/dialect/kernel/dialect.cpp:65, passed through to
  * task.comm.moe_dispatch by src/device/device.cpp:143-147). */
@@ -249,6 +249,46 @@ int kvm_sm100_ep_combine(const kvm_ep_peers* peers, const int32_t* topk_idx,
                          const int32_t* pos, const int32_t* offsets,
                          const int32_t* send_base, const float* topk_w, void* out,
                          int T, int64_t cap_rows, kvm_stream_t stream);
+
+/* Overlapped form of the same exchange: the all-to-all rides inside the
+ * grouped GEMMs, so NVLink transfers overlap the tensor-core work tile by
+ * tile. One call of the layer on each rank (same epoch on all ranks):
+ *   kvm_sm100_ep_prepare          count exchange (as kvm_sm100_ep_counts) and
+ *                                 the call's segment table and return map;
+ *   kvm_sm100_ep_scatter_local    rows routed to this rank's own experts;
+ *   kvm_sm100_ep_dispatch_gate_up the dispatch of the other rows (peer stores
+ *                                 by extra warps of the GEMM) fused with the
+ *                                 grouped SiLU-gate GEMM, which starts a
+ *                                 local expert's tiles as soon as every rank's
+ *                                 rows for it have arrived;
+ *   kvm_sm100_ep_down_push        the grouped down GEMM whose epilogue stores
+ *                                 each output row straight into the result rows
+ *                                 of the rank that routed the token (peer
+ *                                 stores), then raises every rank's outputs flag;
+ *   kvm_sm100_ep_wait(slot 2)     outputs of every rank's experts have arrived;
+ *   kvm_sm100_moe_combine         on this rank's own y buffer, locally.
+ * In this form y[r] holds rank r's result rows [T*k, H] in rank r's permuted
+ * order (cap_rows rows suffice), and flags[r] needs 3*world + E words (one
+ * per local expert and source rank after the three slots). Bit-identical to
+ * kvm_sm100_moe_* on one GPU. workspace: kvm_sm100_ep_overlap_workspace(E,
+ * cap_rows) bytes of this rank's device memory. Executes the same kernel ops
+ * (src/ir/dialect/kernel/ops.h:87-88) as the serial exchange above. */
+int64_t kvm_sm100_ep_overlap_workspace(int E, int64_t cap_rows);
+int kvm_sm100_ep_prepare(const kvm_ep_peers* peers, const int32_t* offsets,
+                         int32_t* send_base, int32_t* local_offsets, void* workspace,
+                         int64_t cap_rows, uint32_t epoch, kvm_stream_t stream);
+int kvm_sm100_ep_scatter_local(const kvm_ep_peers* peers, const void* x,
+                               const int32_t* src_token, const int32_t* offsets,
+                               const int32_t* send_base, int T, int64_t cap_rows,
+                               kvm_stream_t stream);
+int kvm_sm100_ep_dispatch_gate_up(const kvm_ep_peers* peers, const void* x,
+                                  const int32_t* src_token, const int32_t* offsets,
+                                  const int32_t* send_base, const int32_t* local_offsets,
+                                  const void* W13, void* h, int F, int64_t cap_rows,
+                                  void* workspace, uint32_t epoch, kvm_stream_t stream);
+int kvm_sm100_ep_down_push(const kvm_ep_peers* peers, const void* h, const void* W2,
+                           const int32_t* local_offsets, int F, int64_t cap_rows,
+                           void* workspace, uint32_t epoch, kvm_stream_t stream);
 
 /* ---------------------------------------------------------------- FP8 --- */
 

@@ -75,6 +75,12 @@ SIGNATURES = {
     "kvm_sm100_ep_wait": (_I, [_P, _I, C.c_uint32, _P]),
     "kvm_sm100_ep_signal": (_I, [_P, _I, C.c_uint32, _P]),
     "kvm_sm100_ep_combine": (_I, [_P, _P, _P, _P, _P, _P, _P, _I, _I64, _P]),
+    "kvm_sm100_ep_overlap_workspace": (_I64, [_I, _I64]),
+    "kvm_sm100_ep_prepare": (_I, [_P, _P, _P, _P, _P, _I64, C.c_uint32, _P]),
+    "kvm_sm100_ep_scatter_local": (_I, [_P, _P, _P, _P, _P, _I, _I64, _P]),
+    "kvm_sm100_ep_dispatch_gate_up": (_I, [_P, _P, _P, _P, _P, _P, _P, _P, _I, _I64, _P,
+                                           C.c_uint32, _P]),
+    "kvm_sm100_ep_down_push": (_I, [_P, _P, _P, _P, _I, _I64, _P, C.c_uint32, _P]),
     "kvm_sm100_gemm_fp8_workspace": (_I64, [_I, _I, _I]),
     "kvm_sm100_gemm_fp8_blockscaled": (_I, [_P, _P, _P, _P, _P, _I64, _I, _I, _I, _P, _I64,
                                             _P]),

@@ -27,6 +27,7 @@
 
 #include <cstring>
 
+#include "ep_layout.h"
 #include "ptx.cuh"
 #include "runtime.h"
 
@@ -34,16 +35,6 @@ namespace kvm {
 namespace {
 
 enum FlagSlot { kFlagCounts = 0, kFlagData = 1, kFlagOutputs = 2 };
-
-__device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-
-__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
-  unsigned v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
 
 // Bounded wait until *flag >= epoch (epochs only grow). False on timeout.
 __device__ bool wait_flag(const unsigned* flag, unsigned epoch) {
@@ -230,6 +221,153 @@ __global__ void __launch_bounds__(256)
   }
 }
 
+// ------------------------------------------- overlapped expert parallel ---
+//
+// ep_prepare: the count exchange of ep_counts, then, for the fused kernels of
+// the call (gemm_pair.cuh, kEpDispatchGateUp / kEpDownPush): zeroed segment
+// and CTA counters, the row prefix of this rank's remote segments in
+// (local expert, peer) order, and for every row this rank will receive the
+// rank and row its result goes back to. One block.
+__global__ void ep_prepare_kernel(const kvm_ep_peers pr, const int* __restrict__ off,
+                                  int* __restrict__ send_base, int* __restrict__ loc_off,
+                                  EpWorkspace ws, long long cap_rows, unsigned epoch,
+                                  int* status) {
+  // tot [E], src_off [P][E], the count matrix [P][E], this rank's offsets
+  // [E+1] and the first received row of each local expert [E/P], all in
+  // shared memory: the scans below read no global memory
+  extern __shared__ int sm[];
+  int* tot = sm;
+  int* src_off = sm + pr.E;
+  int* scnt = src_off + pr.world * pr.E;
+  int* soff = scnt + pr.world * pr.E;
+  int* gstart = soff + pr.E + 1;
+  const int P = pr.world, E = pr.E, me = pr.rank, epr = E / P;
+  for (int i = threadIdx.x; i < P * E; i += blockDim.x) {
+    const int d = i / E, e = i - d * E;
+    reinterpret_cast<int*>(pr.cnt[d])[me * E + e] = off[e + 1] - off[e];
+  }
+  for (int i = threadIdx.x; i < E; i += blockDim.x) ws.seg_ctr[i] = 0;
+  if (threadIdx.x == 0) *ws.done_ctr = 0;
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x < P) st_release_sys(flag_of(pr, threadIdx.x, kFlagCounts, me), epoch);
+  __shared__ int failed;
+  if (threadIdx.x == 0) failed = 0;
+  __syncthreads();
+  if (threadIdx.x < P &&
+      !wait_flag(flag_of(pr, me, kFlagCounts, threadIdx.x), epoch)) {
+    atomicOr(status, kDevWaitTimeout);
+    failed = 1;
+  }
+  __syncthreads();
+  if (failed) return;
+  {
+    const int* gcnt = reinterpret_cast<const int*>(pr.cnt[me]);  // [P][E], all rows in
+    for (int i = threadIdx.x; i < P * E; i += blockDim.x) scnt[i] = gcnt[i];
+    for (int i = threadIdx.x; i <= E; i += blockDim.x) soff[i] = off[i];
+  }
+  __syncthreads();
+  const int* cnt = scnt;
+  for (int e = threadIdx.x; e < E; e += blockDim.x) {
+    int s = 0;
+    for (int r = 0; r < P; ++r) s += cnt[r * E + e];
+    tot[e] = s;
+  }
+  if (threadIdx.x < P) {  // every source's permuted offsets
+    int acc = 0;
+    for (int e = 0; e < E; ++e) {
+      src_off[threadIdx.x * E + e] = acc;
+      acc += cnt[threadIdx.x * E + e];
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int acc = 0;
+    for (int le = 0; le < epr; ++le) {
+      loc_off[le] = acc;
+      gstart[le] = acc;
+      acc += tot[me * epr + le];
+    }
+    loc_off[epr] = acc;
+    if (acc > cap_rows) atomicOr(status, kDevBadInput);
+    int q = 0;  // remote segments of this rank's rows, (local expert, peer) order
+    const int nseg = epr * (P - 1);
+    for (int sg = 0; sg < nseg; ++sg) {
+      ws.seg_prefix[sg] = q;
+      const int le = sg / (P - 1);
+      const int d = (me + 1 + sg % (P - 1)) % P;
+      const int e = d * epr + le;
+      q += soff[e + 1] - soff[e];
+    }
+    ws.seg_prefix[nseg] = q;
+  }
+  // where this rank's rows of expert e start in the owner's receive buffer:
+  // after the owner's earlier local experts, then after lower source ranks
+  for (int e = threadIdx.x; e < E; e += blockDim.x) {
+    const int d = e / epr, le = e - d * epr;
+    int run = 0, before = 0;
+    for (int x = 0; x < le; ++x) run += tot[d * epr + x];
+    for (int r = 0; r < me; ++r) before += cnt[r * E + e];
+    send_base[e] = run + before;
+  }
+  __syncthreads();
+  // where each received row's result goes: rank s, row src_off[s][e] + j
+  for (int le = 0; le < epr; ++le) {
+    const int e = me * epr + le;
+    int row = gstart[le];  // first received row of (le, source 0)
+    for (int s = 0; s < P; ++s) {
+      const int n = cnt[s * E + e];
+      const int so = src_off[s * E + e];
+      for (int j = threadIdx.x; j < n; j += blockDim.x)
+        if (row + j < cap_rows) ws.push_row[row + j] = (s << 28) | (so + j);
+      row += n;
+    }
+  }
+}
+
+// The rows this rank routes to its own experts, copied into its own receive
+// buffer (the fused dispatch kernel sends only the other ranks' rows). These
+// rows are a contiguous range of the permuted order (the local experts'
+// groups); one warp per row, lanes on 16-byte vectors with every load of a
+// pass issued before its stores.
+__global__ void __launch_bounds__(256)
+    ep_scatter_local_kernel(const kvm_ep_peers pr, const uint4* __restrict__ x,
+                            const int* __restrict__ src_token, const int* __restrict__ off,
+                            const int* __restrict__ send_base, long long cap_rows,
+                            int* status) {
+  const int epr = pr.E / pr.world, e0 = pr.rank * epr;
+  const int r0 = off[e0], r1 = off[e0 + epr];
+  const int lane = threadIdx.x % 32;
+  const int r = r0 + static_cast<int>(blockIdx.x) * 8 + static_cast<int>(threadIdx.x / 32);
+  if (r >= r1) return;
+  int lo = e0, hi = e0 + epr - 1;  // local expert of row r: largest e with off[e] <= r
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (off[mid] <= r) lo = mid; else hi = mid - 1;
+  }
+  const long long row = send_base[lo] + (r - off[lo]);
+  if (row < 0 || row >= cap_rows) {
+    if (lane == 0) atomicOr(status, kDevBadInput);
+    return;
+  }
+  const int rv = pr.H / 8;
+  const uint4* src = x + static_cast<long long>(src_token[r]) * rv;
+  uint4* dst = reinterpret_cast<uint4*>(pr.recv[pr.rank]) + row * rv;
+  for (int v0 = 0; v0 < rv; v0 += 32 * 8) {
+    uint4 buf[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int v = v0 + u * 32 + lane;
+      if (v < rv) buf[u] = __ldg(src + v);
+    }
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int v = v0 + u * 32 + lane;
+      if (v < rv) dst[v] = buf[u];
+    }
+  }
+}
+
 int check_peers(const kvm_ep_peers* pr) {
   if (!pr) return fail(KVM_ERR_INVALID_ARG, "ep: NULL peer table");
   if (pr->world < 1 || pr->world > KVM_EP_MAX_RANKS || pr->rank < 0 ||
@@ -352,6 +490,53 @@ extern "C" int kvm_sm100_ep_combine(const kvm_ep_peers* pr, const int32_t* topk_
   if (!dev) return KVM_ERR_CUDA;
   ep_combine_kernel<<<T, 256, 0, static_cast<cudaStream_t>(stream)>>>(
       *pr, topk_idx, pos, offsets, send_base, topk_w, static_cast<uint4*>(out), cap_rows,
+      dev->status);
+  KVM_CUDA_TRY(cudaGetLastError());
+  return KVM_OK;
+}
+
+extern "C" int64_t kvm_sm100_ep_overlap_workspace(int E, int64_t cap_rows) {
+  if (E <= 0 || cap_rows <= 0) return 0;
+  return ep_workspace_bytes(E, cap_rows);
+}
+
+extern "C" int kvm_sm100_ep_prepare(const kvm_ep_peers* pr, const int32_t* offsets,
+                                    int32_t* send_base, int32_t* local_offsets,
+                                    void* workspace, int64_t cap_rows, uint32_t epoch,
+                                    kvm_stream_t stream) {
+  if (int rc = check_peers(pr); rc != KVM_OK) return rc;
+  if (!offsets || !send_base || !local_offsets || !workspace || cap_rows <= 0 ||
+      cap_rows >= (1ll << 28) || epoch == 0)
+    return fail(KVM_ERR_INVALID_ARG, "ep_prepare: NULL pointer, cap_rows or epoch 0");
+  const DeviceInfo* dev = device_info();
+  if (!dev) return KVM_ERR_CUDA;
+  const EpWorkspace ws = ep_workspace(workspace, pr->E, cap_rows);
+  const size_t smem = sizeof(int) * (static_cast<size_t>(pr->E) * (1 + 2 * pr->world) +
+                                     pr->E + 1 + pr->E / pr->world);
+  if (smem > 48 * 1024)
+    KVM_CUDA_TRY(cudaFuncSetAttribute(ep_prepare_kernel,
+                                      cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      static_cast<int>(smem)));
+  ep_prepare_kernel<<<1, 1024, smem, static_cast<cudaStream_t>(stream)>>>(
+      *pr, offsets, send_base, local_offsets, ws, cap_rows, epoch, dev->status);
+  KVM_CUDA_TRY(cudaGetLastError());
+  return KVM_OK;
+}
+
+extern "C" int kvm_sm100_ep_scatter_local(const kvm_ep_peers* pr, const void* x,
+                                          const int32_t* src_token, const int32_t* offsets,
+                                          const int32_t* send_base, int T, int64_t cap_rows,
+                                          kvm_stream_t stream) {
+  if (int rc = check_peers(pr); rc != KVM_OK) return rc;
+  if (T <= 0 || !x || !aligned16(x) || !src_token || !offsets || !send_base ||
+      cap_rows <= 0)
+    return fail(KVM_ERR_INVALID_ARG, "ep_scatter_local: bad argument");
+  const DeviceInfo* dev = device_info();
+  if (!dev) return KVM_ERR_CUDA;
+  const long long rows = static_cast<long long>(T) * pr->k;  // at most this many local
+  ep_scatter_local_kernel<<<static_cast<unsigned>((rows + 7) / 8), 256, 0,
+                            static_cast<cudaStream_t>(stream)>>>(
+      *pr, static_cast<const uint4*>(x), src_token, offsets, send_base, cap_rows,
       dev->status);
   KVM_CUDA_TRY(cudaGetLastError());
   return KVM_OK;

@@ -6,6 +6,7 @@
 #include <cstring>
 #include <mutex>
 
+#include "ep_layout.h"
 #include "gemm_bf16.cuh"
 #include "gemm_pair.cuh"
 #include "router.cuh"
@@ -30,7 +31,7 @@ int launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tb2,
 
 // SM pairs that can be resident at once for the pair kernel (clusters of 2
 // need two free SMs of one GPC), cached per device and epilogue.
-template <int EPI>
+template <int EPI, int EP = kEpNone>
 int pair_clusters(int* out) {
   static std::mutex mu;
   static int cached[64] = {0};
@@ -41,7 +42,7 @@ int pair_clusters(int* out) {
     *out = cached[dev];
     return KVM_OK;
   }
-  auto kern = gemm_pair_kernel<EPI>;
+  auto kern = gemm_pair_kernel<EPI, EP>;
   constexpr size_t smem = gemm_pair_smem_bytes();
   KVM_CUDA_TRY(cudaFuncSetAttribute(
       kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
@@ -49,7 +50,7 @@ int pair_clusters(int* out) {
   if (!d) return KVM_ERR_CUDA;
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(2 * (d->sm_count / 2));
-  cfg.blockDim = dim3(kPairThreads);
+  cfg.blockDim = dim3(pair_threads(EP));
   cfg.dynamicSmemBytes = smem;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -68,17 +69,17 @@ int pair_clusters(int* out) {
 }
 
 // Launch the pair kernel on min(resident pairs, upper bound of pair tiles).
-template <int EPI>
+template <int EPI, int EP = kEpNone>
 int launch_pair(const PairMaps& maps, const PairParams& p, long long max_tiles,
-                cudaStream_t st) {
+                cudaStream_t st, const PairEp& ep = PairEp{}) {
   int ncl = 0;
-  int rc = pair_clusters<EPI>(&ncl);
+  int rc = pair_clusters<EPI, EP>(&ncl);
   if (rc != KVM_OK) return rc;
   if (max_tiles < ncl) ncl = int(max_tiles > 0 ? max_tiles : 1);
-  auto kern = gemm_pair_kernel<EPI>;
+  auto kern = gemm_pair_kernel<EPI, EP>;
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(2 * ncl);
-  cfg.blockDim = dim3(kPairThreads);
+  cfg.blockDim = dim3(pair_threads(EP));
   cfg.dynamicSmemBytes = gemm_pair_smem_bytes();
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
@@ -88,7 +89,7 @@ int launch_pair(const PairMaps& maps, const PairParams& p, long long max_tiles,
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  KVM_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, maps, p));
+  KVM_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, maps, p, ep));
   return KVM_OK;
 }
 
@@ -362,11 +363,6 @@ extern "C" int kvm_sm100_moe_router_topk(const void* x, const void* Wr,
   int tr = (cdiv(T, dev->sm_count) + 7) & ~7;
   tr = tr < 32 ? 32 : tr > 128 ? 128 : tr;
   p.tile_rows = tr;
-  // K chunks: as many accumulators as TMEM holds (512 columns), none empty.
-  const int kb_total = cdiv(H, kRouterBK);
-  int nch = std::min(512 / BN, kb_total);
-  const int kpc = cdiv(kb_total, nch);
-  p.nch = cdiv(kb_total, kpc);
   const int tiles = cdiv(T, tr);
   const int grid = tiles < dev->sm_count ? tiles : dev->sm_count;
   CUtensorMap tx, tw;
@@ -380,4 +376,109 @@ extern "C" int kvm_sm100_moe_router_topk(const void* x, const void* Wr,
   if (BN == 64) return launch_router<64>(tx, tw, p, grid, st);
   if (BN == 128) return launch_router<128>(tx, tw, p, grid, st);
   return launch_router<256>(tx, tw, p, grid, st);
+}
+
+// ------------------------------------------- overlapped expert parallel ---
+// The dispatch all-to-all fused with the gate/up GEMM, and the down GEMM
+// fused with the combine all-to-all (gemm_pair.cuh, kEpDispatchGateUp /
+// kEpDownPush), over the peer buffers of an expert-parallel group.
+
+namespace kvm {
+namespace {
+
+int ep_common(const kvm_ep_peers* pr, int64_t cap_rows, const void* workspace,
+              uint32_t epoch, PairEp* ep) {
+  if (!pr || pr->world < 1 || pr->world > KVM_EP_MAX_RANKS || pr->rank < 0 ||
+      pr->rank >= pr->world || pr->E < 1 || pr->E % pr->world != 0 || pr->H % 8 != 0)
+    return fail(KVM_ERR_INVALID_ARG, "ep gemm: bad peer table");
+  if (!workspace || cap_rows <= 0 || cap_rows >= (1ll << 28) || epoch == 0)
+    return fail(KVM_ERR_INVALID_ARG, "ep gemm: NULL workspace, bad cap_rows or epoch 0");
+  if (pr->E / pr->world > kMaxGroups)
+    return fail(KVM_ERR_UNSUPPORTED, "ep gemm: more than 256 experts per rank");
+  *ep = PairEp{};
+  ep->P = pr->world;
+  ep->me = pr->rank;
+  ep->epr = pr->E / pr->world;
+  ep->epoch = epoch;
+  for (int r = 0; r < pr->world; ++r) {
+    if (!pr->recv[r] || !pr->y[r] || !pr->flags[r])
+      return fail(KVM_ERR_INVALID_ARG, "ep gemm: missing peer buffer");
+    ep->flags[r] = static_cast<unsigned*>(pr->flags[r]);
+    ep->recv[r] = pr->recv[r];
+    ep->push_base[r] = pr->y[r];
+  }
+  const EpWorkspace ws = ep_workspace(const_cast<void*>(workspace), pr->E, cap_rows);
+  ep->seg_ctr = ws.seg_ctr;
+  ep->seg_prefix = ws.seg_prefix;
+  ep->nseg = ep->epr * (pr->world - 1);
+  ep->push_row = ws.push_row;
+  ep->done_ctr = ws.done_ctr;
+  return KVM_OK;
+}
+
+}  // namespace
+}  // namespace kvm
+
+extern "C" int kvm_sm100_ep_dispatch_gate_up(const kvm_ep_peers* pr, const void* x,
+                                             const int32_t* src_token,
+                                             const int32_t* offsets,
+                                             const int32_t* send_base,
+                                             const int32_t* local_offsets,
+                                             const void* W13, void* Hout, int F,
+                                             int64_t cap_rows, void* workspace,
+                                             uint32_t epoch, kvm_stream_t stream) {
+  PairEp ep;
+  KVM_TRY(ep_common(pr, cap_rows, workspace, epoch, &ep));
+  if (F <= 0 || F % 128 != 0)
+    return fail(KVM_ERR_INVALID_ARG, "ep dispatch gate/up: F must be a multiple of 128");
+  if (!src_token || !offsets || !send_base || !local_offsets)
+    return fail(KVM_ERR_INVALID_ARG, "ep dispatch gate/up: NULL index array");
+  KVM_TRY(check_ptr(x, "ep dispatch gate/up: x"));
+  KVM_TRY(check_ptr(W13, "ep dispatch gate/up: W13"));
+  KVM_TRY(check_ptr(Hout, "ep dispatch gate/up: H"));
+  const DeviceInfo* dev = device_info();
+  if (!dev) return KVM_ERR_CUDA;
+  const int H = pr->H, G = ep.epr, N = 2 * F;
+  ep.x = static_cast<const uint4*>(x);
+  ep.row_vecs = H / 8;
+  ep.src_token = src_token;
+  ep.offsets = offsets;
+  ep.send_base = send_base;
+  PairParams pp{};
+  pp.rows = static_cast<int>(cap_rows); pp.N = N; pp.K = H;
+  pp.num_groups = G; pp.offsets = local_offsets;
+  pp.D = Hout; pp.ldd = F; pp.C = nullptr; pp.ldc = 0;
+  pp.status = dev->status;
+  PairMaps maps;
+  KVM_TRY(encode_pair_maps(&maps, pr->recv[pr->rank], H, pp.rows, W13, (long long)N * G, H));
+  // Every resident pair is launched: the dispatch warps of all CTAs must run
+  // whatever the number of GEMM tiles.
+  return launch_pair<kEpiSilu, kEpDispatchGateUp>(maps, pp, 1ll << 30,
+                                                   static_cast<cudaStream_t>(stream), ep);
+}
+
+extern "C" int kvm_sm100_ep_down_push(const kvm_ep_peers* pr, const void* Hact,
+                                      const void* W2, const int32_t* local_offsets, int F,
+                                      int64_t cap_rows, void* workspace, uint32_t epoch,
+                                      kvm_stream_t stream) {
+  PairEp ep;
+  KVM_TRY(ep_common(pr, cap_rows, workspace, epoch, &ep));
+  if (F <= 0 || F % 8 != 0)
+    return fail(KVM_ERR_INVALID_ARG, "ep down push: F must be a multiple of 8");
+  if (!local_offsets) return fail(KVM_ERR_INVALID_ARG, "ep down push: NULL offsets");
+  KVM_TRY(check_ptr(Hact, "ep down push: H"));
+  KVM_TRY(check_ptr(W2, "ep down push: W2"));
+  const DeviceInfo* dev = device_info();
+  if (!dev) return KVM_ERR_CUDA;
+  const int H = pr->H, G = ep.epr;
+  PairParams pp{};
+  pp.rows = static_cast<int>(cap_rows); pp.N = H; pp.K = F;
+  pp.num_groups = G; pp.offsets = local_offsets;
+  pp.D = nullptr; pp.ldd = H; pp.C = nullptr; pp.ldc = 0;
+  pp.status = dev->status;
+  PairMaps maps;
+  KVM_TRY(encode_pair_maps(&maps, Hact, F, pp.rows, W2, (long long)H * G, F));
+  // All resident pairs, so that the last CTA to finish raises the flags.
+  return launch_pair<kEpiBf16, kEpDownPush>(maps, pp, 1ll << 30,
+                                             static_cast<cudaStream_t>(stream), ep);
 }

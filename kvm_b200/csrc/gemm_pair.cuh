@@ -78,6 +78,156 @@ struct PairParams {
   int* status;
 };
 
+// Expert-parallel forms of the kernel (kEp* below), for the layer whose
+// experts are sharded over the GPUs of one node (one process per GPU, peer
+// memory mapped between them):
+//
+// kEpDispatchGateUp -- the dispatch all-to-all fused with the gate/up GEMM.
+//   Four extra warps per CTA store this rank's routed token rows into the
+//   owners' receive buffers (peer stores), local expert by local expert, and
+//   after each (owner, local expert) segment is complete raise that owner's
+//   flag for it. The producer of every CTA waits, before the first tile of a
+//   group, until every other rank has raised its flag for that group, so the
+//   MMAs of expert 0 run while the rows of later experts are still crossing
+//   NVLink. Rows a rank routes to its own experts are written before the
+//   launch (a stream-ordered kernel), so no CTA waits on another CTA of its
+//   own GPU: the only waits are on other GPUs, whose CTAs all stay resident
+//   (the grid is the resident pair count).
+// kEpDownPush -- the down GEMM fused with the combine all-to-all: the
+//   epilogue stores each output row straight into the result rows of the rank
+//   that routed the token (peer stores, at the row of its permuted order), and
+//   the last CTA to finish raises every rank's outputs flag.
+enum PairEpMode : int { kEpNone = 0, kEpDispatchGateUp = 1, kEpDownPush = 2 };
+
+constexpr int kPairDispatchWarps = 4;
+constexpr int pair_threads(int ep) {
+  return kPairThreads + (ep == kEpDispatchGateUp ? 32 * kPairDispatchWarps : 0);
+}
+
+struct PairEp {
+  int P, me, epr;                 // ranks, this rank, experts per rank
+  unsigned epoch;                 // this call's epoch (flags hold epochs)
+  unsigned* flags[8];             // every rank's flag words
+  // kEpDispatchGateUp
+  const uint4* x;                 // this rank's tokens [T, H]
+  int row_vecs;                   // H / 8
+  const int* src_token;           // [T*k] token of each permuted row
+  const int* offsets;             // [E+1] this rank's per-expert row offsets
+  const int* send_base;           // [E] first row in the owner's receive buffer
+  const int* seg_prefix;          // [nseg+1] rows of the remote segments
+  int nseg;                       // epr * (P - 1): segment sg = (le, k-th peer)
+  int* seg_ctr;                   // [nseg] rows stored so far (zero at launch)
+  void* recv[8];                  // every rank's receive buffer
+  // kEpDownPush
+  void* push_base[8];             // every rank's result rows [T*k, H]
+  const int* push_row;            // [rows] (source rank << 28) | row there
+  int* done_ctr;                  // CTAs finished (zero at launch)
+};
+
+// Flag words of one rank: [0, P) counts, [P, 2P) data (whole rank),
+// [2P, 3P) outputs, then [3P + le*P + src] the per-group data flags.
+__device__ __forceinline__ unsigned* ep_group_flag(const PairEp& ep, int owner, int le,
+                                                   int src) {
+  return ep.flags[owner] + 3 * ep.P + le * ep.P + src;
+}
+
+// Bounded wait until every other rank's flag for group g holds this epoch,
+// then order the TMA loads that follow after those acquires.
+__device__ __forceinline__ bool ep_wait_group(const PairEp& ep, int g,
+                                              volatile int* abort) {
+  for (int s = 0; s < ep.P; ++s) {
+    if (s == ep.me) continue;
+    const unsigned* f = ep_group_flag(ep, ep.me, g, s);
+    if (ld_acquire_sys(f) >= ep.epoch) continue;
+    const uint64_t t0 = globaltimer_ns();
+    while (ld_acquire_sys(f) < ep.epoch) {
+      if (*abort) return false;
+      if (globaltimer_ns() - t0 > kWaitTimeoutNs) {
+        *abort = 1;
+        return false;
+      }
+      __nanosleep(128);
+    }
+  }
+  fence_proxy_async_global();
+  return true;
+}
+
+__device__ __forceinline__ void ep_raise_segment(const PairEp& ep, int sg) {
+  const int le = sg / (ep.P - 1);
+  const int d = (ep.me + 1 + sg % (ep.P - 1)) % ep.P;
+  st_release_sys(ep_group_flag(ep, d, le, ep.me), ep.epoch);
+}
+
+// The dispatch warps: this rank's rows for other ranks' experts, in the
+// order (local expert, owner), cut in chunks of 2 rows dealt round-robin to
+// every dispatch warp of the grid. A warp copies a chunk (row by row, each
+// lane 16-byte vectors), fences, then credits the rows to their segments; the
+// warp that completes a segment raises the owner's flag for it. Small chunks
+// keep the rows in flight at any moment (2 x the dispatch warps) to a few
+// local experts' worth, so the first experts' rows arrive, and their GEMM
+// tiles start, long before the whole exchange is over; the copy rate stays
+// bound by NVLink, not by the fences.
+__device__ void ep_dispatch_rows(const PairEp& ep, int w, int nw, int lane) {
+  if (ep.P < 2) return;
+  const int nseg = ep.nseg;
+  const int* sp = ep.seg_prefix;
+  if (w == 0)
+    for (int sg = lane; sg < nseg; sg += 32)
+      if (sp[sg + 1] == sp[sg]) ep_raise_segment(ep, sg);
+  constexpr int RC = 2;
+  const int total = sp[nseg];
+  const int n_chunks = (total + RC - 1) / RC;
+  const int rv = ep.row_vecs;
+  for (int ch = w; ch < n_chunks; ch += nw) {
+    const int q0 = ch * RC, q1 = min(total, q0 + RC);
+    int lo = 0, hi = nseg - 1;  // segment of q0: largest sg with sp[sg] <= q0
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (sp[mid] <= q0) lo = mid; else hi = mid - 1;
+    }
+    const int sg0 = lo;
+    int sg = sg0;
+    for (int q = q0; q < q1; ++q) {
+      while (q >= sp[sg + 1]) ++sg;
+      const int le = sg / (ep.P - 1);
+      const int d = (ep.me + 1 + sg % (ep.P - 1)) % ep.P;
+      const int e = d * ep.epr + le;
+      const int j = q - sp[sg];
+      const long long tok = ep.src_token[ep.offsets[e] + j];
+      const uint4* src = ep.x + tok * rv;
+      uint4* dst = static_cast<uint4*>(ep.recv[d]) +
+                   static_cast<long long>(ep.send_base[e] + j) * rv;
+      for (int v0 = 0; v0 < rv; v0 += 32 * 8) {
+        uint4 buf[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const int v = v0 + u * 32 + lane;
+          if (v < rv) buf[u] = __ldg(src + v);
+        }
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const int v = v0 + u * 32 + lane;
+          if (v < rv) dst[v] = buf[u];
+        }
+      }
+    }
+    __threadfence_system();
+    __syncwarp();
+    if (lane == 0) {
+      for (int s2 = sg0; s2 <= sg; ++s2) {
+        const int n = min(q1, sp[s2 + 1]) - max(q0, sp[s2]);
+        if (n <= 0) continue;
+        if (atomicAdd(&ep.seg_ctr[s2], n) + n == sp[s2 + 1] - sp[s2]) {
+          __threadfence_system();
+          ep_raise_segment(ep, s2);
+        }
+      }
+    }
+    __syncwarp();
+  }
+}
+
 constexpr size_t gemm_pair_smem_bytes() {
   return 1024 + static_cast<size_t>(kPairStages) * kPairStageBytes +
          kPairUBytes + (2 * kPairStages + 2 + 2 + 1 + 4) * 8 + 16 +
@@ -97,10 +247,14 @@ struct PairTile {
   int tn;      // MMA N (multiple of 16, >= valid)
 };
 
-template <int EPI>
-__global__ void __launch_bounds__(kPairThreads, 1)
-    gemm_pair_kernel(const __grid_constant__ PairMaps maps, const PairParams p) {
+template <int EPI, int EP = kEpNone>
+__global__ void __launch_bounds__(pair_threads(EP), 1)
+    gemm_pair_kernel(const __grid_constant__ PairMaps maps, const PairParams p,
+                     const __grid_constant__ PairEp ep) {
   static_assert(EPI == kEpiBf16 || EPI == kEpiSilu, "pair GEMM epilogues");
+  static_assert(EP == kEpNone || (EP == kEpDispatchGateUp && EPI == kEpiSilu) ||
+                    (EP == kEpDownPush && EPI == kEpiBf16),
+                "expert-parallel forms: dispatch + gate/up, down + push");
   constexpr int BK = kPairBK;
 
   extern __shared__ uint8_t smem_raw[];
@@ -209,8 +363,15 @@ __global__ void __launch_bounds__(kPairThreads, 1)
       int s = 0;
       uint32_t ph = 0;
       bool ok = true;
+      int ready_g = -1;  // groups whose rows from every rank have arrived
       for (int t = cl0; t < total_tiles && ok; t += ncl) {
         const PairTile tl = map_tile(t);
+        if constexpr (EP == kEpDispatchGateUp) {
+          if (tl.g > ready_g) {
+            if (!ep_wait_group(ep, tl.g, abort_flag)) { ok = false; break; }
+            ready_g = tl.g;
+          }
+        }
         // rows this CTA stages: the smallest box covering tn/2 token rows
         int box = 0;
         while ((128 >> box) >= tl.tn && box < 4) ++box;
@@ -271,6 +432,11 @@ __global__ void __launch_bounds__(kPairThreads, 1)
       volatile int local_abort = 0;
       mbar_wait(drain, 0, &local_abort);
     }
+  } else if (EP == kEpDispatchGateUp && warp >= 2 + kPairEpiWarps) {
+    // -------------------------------------------------- dispatch warps
+    ep_dispatch_rows(ep, static_cast<int>(blockIdx.x) * kPairDispatchWarps +
+                             (warp - 2 - kPairEpiWarps),
+                     static_cast<int>(gridDim.x) * kPairDispatchWarps, lane);
   } else {
     // -------------------------------------------------- epilogue warps
     const int q = warp & 3;          // TMEM lane quarter this warp may access
@@ -303,7 +469,24 @@ __global__ void __launch_bounds__(kPairThreads, 1)
           tmem_ld32(t_row + c * 32, r);
           tmem_wait_ld();
           const int nv = min(32, tl.valid - c * 32);
-          if (col_ok) {
+          if constexpr (EP == kEpDownPush) {
+            // row i of the chunk goes to rank (m >> 28), row (m & 0x0FFFFFFF)
+            // of its result rows: lane i forms that row's address, every lane
+            // then adds its column
+            uintptr_t rowp = 0;
+            if (lane < nv) {
+              const int m = __ldg(ep.push_row + tl.r0 + c * 32 + lane);
+              rowp = reinterpret_cast<uintptr_t>(ep.push_base[m >> 28]) +
+                     static_cast<uintptr_t>(m & 0x0FFFFFFF) * (p.ldd * 2);
+            }
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              const uintptr_t base = __shfl_sync(0xffffffffu, rowp, i);
+              if (i < nv && col_ok)
+                reinterpret_cast<__nv_bfloat16*>(base)[col] =
+                    __float2bfloat16_rn(__uint_as_float(r[i]));
+            }
+          } else if (col_ok) {
 #pragma unroll
             for (int i = 0; i < 32; ++i) {
               if (i < nv) {
@@ -355,7 +538,16 @@ __global__ void __launch_bounds__(kPairThreads, 1)
     }
   }
 
+  if constexpr (EP == kEpDownPush) __threadfence_system();  // this CTA's pushed rows
   __syncthreads();
+  if constexpr (EP == kEpDownPush) {
+    if (threadIdx.x == 0 && !*abort_flag) {
+      if (atomicAdd(ep.done_ctr, 1) == static_cast<int>(gridDim.x) - 1) {
+        __threadfence_system();  // every CTA's rows are out: tell every rank
+        for (int r = 0; r < ep.P; ++r) st_release_sys(ep.flags[r] + 2 * ep.P + ep.me, ep.epoch);
+      }
+    }
+  }
   if (*abort_flag) {
     // Let copies and arrivals already in flight land before the pair tears
     // down (their completion is counted on the even CTA's barriers).

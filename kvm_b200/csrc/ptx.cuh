@@ -280,6 +280,25 @@ __device__ __forceinline__ void fence_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
+// System-scope release store / acquire load of a 32-bit flag (a word that
+// another GPU reads or writes through peer memory).
+__device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Order this thread's earlier generic-proxy accesses (e.g. the acquire of a
+// flag that guards data other GPUs stored) before its later async-proxy
+// accesses (TMA loads of that data).
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
 // 2^x on the special-function unit (ex2.approx, flush-to-zero).
 __device__ __forceinline__ float ex2_approx(float x) {
   float y;

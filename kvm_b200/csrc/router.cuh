@@ -2,25 +2,24 @@
 // kernel.comm.moe_dispatch): logits[T, E] = x[T, H] . Wr^T in fp32 on the
 // tensor cores, then per token the softmax over the E logits and the k largest.
 //
-// The x rows stream from HBM once; the router weights (E x H, 512 KB at E = 64,
-// H = 4096) are read by every CTA. If all CTAs walked K in the same order they
-// would all read the same few KB of weights at the same moment, and those L2
-// lines, not HBM, would set the pace. So K is cut into NCH chunks, each
-// accumulated into a TMEM accumulator of its own, and CTA b works through the
-// chunks starting at chunk b mod NCH: at any moment the CTAs spread over NCH
-// regions of the weights. The epilogue adds the chunk accumulators in chunk
-// order (((c0 + c1) + c2) + ...), so a token's logits depend only on its own
-// row and H -- not on which tile or CTA computed it, nor on the token count.
-//
 //   warp 0 (one lane)  TMA producer: per K block one box of x (TR rows) and
 //                      one box of Wr (BN rows; rows past E read as zero)
-//   warp 1 (one lane)  MMA issuer: tcgen05.mma kind::f16, M = 128, N = BN,
-//                      into accumulator `chunk` of the tile
+//   warp 1 (one lane)  MMA issuer: tcgen05.mma kind::f16, M = 128, N = BN
+//                      (64, 128 or 256 >= E), K in ascending 64-deep blocks
 //   warps 2..5         epilogue, one thread per token row: logits out, then
-//                      max, top-k and the softmax sum over E
+//                      max, the softmax sum over E and the top-k
 //
 // A tile is TR <= 128 token rows (the MMA is M = 128; TMEM lanes at or past TR
-// are not read back), sized so the tiles cover the SMs.
+// are not read back), sized so the tiles cover the SMs. A token's logits are
+// the same bits whichever tile, CTA or batch computes them: one accumulator,
+// K always in the same order.
+//
+// Measured on B200 (8192 tokens, H 4096, E 64): ~29 us per launch, of which
+// streaming x at the copy rate would be ~10 us; the rest is the fixed cost
+// of one tile per CTA (pipeline fill, epilogue, launch). Walking K from a
+// different chunk in different CTAs (so that they do not all read the same
+// router-weight lines at once) changed nothing (35.3 / 36.2 / 36.7 us per
+// call with 1 / 4 / 8 chunks), so the weights' L2 lines are not the limit.
 #pragma once
 
 #include <cuda_bf16.h>
@@ -35,7 +34,6 @@ constexpr int kRouterBK = 64;
 struct RouterParams {
   int T, E, K, top_k;
   int tile_rows;   // TR, a multiple of 8 in [8, 128]
-  int nch;         // K chunks (each a TMEM accumulator of BN columns)
   float* logits;   // [T, E]
   int* topk_idx;   // [T, k]
   float* topk_w;   // [T, k]
@@ -49,7 +47,6 @@ struct RouterCfg {
   static constexpr uint32_t kStageBytes = kABytes + kBBytes;
   static constexpr int kStages = (196608 / kStageBytes) > 8 ? 8 : (196608 / kStageBytes);
   static constexpr size_t kSmem = 1024 + size_t(kStages) * kStageBytes + (2 * kStages + 3) * 8 + 16;
-  static constexpr int kMaxChunks = 512 / BN;
 };
 
 // Insert (v, i) into the descending top-k list (bv, bi) of n valid entries:
@@ -62,17 +59,21 @@ __device__ __forceinline__ void topk_insert(float (&bv)[8], int (&bi)[8], int& n
   for (int p = 1; p < 8; ++p)
     if (p == k - 1) kth = bv[p];
   if (n >= k && !(v > kth)) return;
+  // v goes before the first smaller entry (or into the first empty slot);
+  // from there on every entry moves down one slot and the last drops out.
   float cv = v;
   int ci = i;
+  bool placed = false;
 #pragma unroll
   for (int p = 0; p < 8; ++p) {
-    if (p < k && (p >= n || bv[p] < cv)) {
+    if (p < k && (placed || p >= n || bv[p] < cv)) {
       const float tv = bv[p];
       const int ti = bi[p];
       bv[p] = cv;
       bi[p] = ci;
       cv = tv;
       ci = ti;
+      placed = true;
     }
   }
   if (n < k) ++n;
@@ -103,10 +104,7 @@ __global__ void __launch_bounds__(kRouterThreads, 1)
   const int TR = p.tile_rows;
   const int tiles = (p.T + TR - 1) / TR;
   const int kb_total = (p.K + BK - 1) / BK;
-  const int nch = p.nch;
-  const int kpc = (kb_total + nch - 1) / nch;   // K blocks per chunk
-  uint32_t tmem_cols = 32;
-  while (tmem_cols < static_cast<uint32_t>(nch * BN)) tmem_cols <<= 1;
+  constexpr uint32_t tmem_cols = BN;
 
   if (threadIdx.x == 0) {
     *abort_flag = 0;
@@ -131,7 +129,6 @@ __global__ void __launch_bounds__(kRouterThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
-  const int first_chunk = static_cast<int>(blockIdx.x) % nch;
 
   if (warp == 0) {
     if (lane == 0) {
@@ -145,19 +142,15 @@ __global__ void __launch_bounds__(kRouterThreads, 1)
       for (int i = 0; i < STAGES; ++i) armed[i] = false;
       for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
         const int row0 = t * TR;
-        for (int j = 0; j < nch && ok; ++j) {
-          const int c = (first_chunk + j) % nch;
-          const int kb1 = min(kb_total, (c + 1) * kpc);
-          for (int kb = c * kpc; kb < kb1; ++kb) {
-            if (!mbar_wait(&empty[s], ph ^ 1, abort_flag)) { ok = false; break; }
-            uint8_t* a_dst = smem + s * C::kStageBytes;
-            mbar_arrive_expect_tx(&full[s], static_cast<uint32_t>(TR + BN) * (BK * 2));
-            armed[s] = true;
-            armed_ph[s] = ph;
-            tma_load_2d(a_dst, &tmX, &full[s], kb * BK, row0);
-            tma_load_2d(a_dst + C::kABytes, &tmW, &full[s], kb * BK, 0);
-            if (++s == STAGES) { s = 0; ph ^= 1; }
-          }
+        for (int kb = 0; kb < kb_total; ++kb) {
+          if (!mbar_wait(&empty[s], ph ^ 1, abort_flag)) { ok = false; break; }
+          uint8_t* a_dst = smem + s * C::kStageBytes;
+          mbar_arrive_expect_tx(&full[s], static_cast<uint32_t>(TR + BN) * (BK * 2));
+          armed[s] = true;
+          armed_ph[s] = ph;
+          tma_load_2d(a_dst, &tmX, &full[s], kb * BK, row0);
+          tma_load_2d(a_dst + C::kABytes, &tmW, &full[s], kb * BK, 0);
+          if (++s == STAGES) { s = 0; ph ^= 1; }
         }
       }
       if (!ok) {
@@ -177,23 +170,18 @@ __global__ void __launch_bounds__(kRouterThreads, 1)
         // one accumulator set: wait until the epilogue has read the last tile's
         if (!mbar_wait(tempty, (it & 1) ^ 1, abort_flag)) { ok = false; break; }
         tc_fence_after();
-        for (int j = 0; j < nch && ok; ++j) {
-          const int c = (first_chunk + j) % nch;
-          const uint32_t d_tmem = tmem_base + c * BN;
-          const int kb0 = c * kpc, kb1 = min(kb_total, (c + 1) * kpc);
-          for (int kb = kb0; kb < kb1; ++kb) {
-            if (!mbar_wait(&full[s], ph, abort_flag)) { ok = false; break; }
-            tc_fence_after();
-            const uint32_t a_addr = smem_u32(smem + s * C::kStageBytes);
-            const uint32_t b_addr = a_addr + C::kABytes;
+        for (int kb = 0; kb < kb_total; ++kb) {
+          if (!mbar_wait(&full[s], ph, abort_flag)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(smem + s * C::kStageBytes);
+          const uint32_t b_addr = a_addr + C::kABytes;
 #pragma unroll
-            for (int k = 0; k < BK / 16; ++k)
-              mma_f16_ss(d_tmem, sdesc_sw128(a_addr + k * 32, 0, 1024),
-                         sdesc_sw128(b_addr + k * 32, 0, 1024), kIdesc,
-                         (kb != kb0 || k != 0) ? 1u : 0u);
-            mma_commit(&empty[s]);
-            if (++s == STAGES) { s = 0; ph ^= 1; }
-          }
+          for (int k = 0; k < BK / 16; ++k)
+            mma_f16_ss(tmem_base, sdesc_sw128(a_addr + k * 32, 0, 1024),
+                       sdesc_sw128(b_addr + k * 32, 0, 1024), kIdesc,
+                       (kb | k) != 0 ? 1u : 0u);
+          mma_commit(&empty[s]);
+          if (++s == STAGES) { s = 0; ph ^= 1; }
         }
         if (ok) mma_commit(tfull);
       }
@@ -224,62 +212,99 @@ __global__ void __launch_bounds__(kRouterThreads, 1)
       }
       int n = 0;
       float mx = -INFINITY;
-      // pass 1: logits (chunk accumulators added in chunk order), max, top-k
-#pragma unroll 1
-      for (int sl = 0; sl < BN / 32; ++sl) {
-        float v[32];
+      float sum = 0.f;
+      if constexpr (BN == 64) {
+        // all 64 logits of the row in registers
+        float v[64];
         {
-          uint32_t r[32];
-          tmem_ld32(t_row + sl * 32, r);
+          uint32_t r0[32], r1[32];
+          tmem_ld32(t_row, r0);
+          tmem_ld32(t_row + 32, r1);
           tmem_wait_ld();
 #pragma unroll
-          for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
-        }
-#pragma unroll 1
-        for (int c = 1; c < nch; ++c) {
-          uint32_t r[32];
-          tmem_ld32(t_row + c * BN + sl * 32, r);
-          tmem_wait_ld();
-#pragma unroll
-          for (int i = 0; i < 32; ++i) v[i] += __uint_as_float(r[i]);
+          for (int i = 0; i < 32; ++i) {
+            v[i] = __uint_as_float(r0[i]);
+            v[32 + i] = __uint_as_float(r1[i]);
+          }
         }
         if (row_ok) {
+          if (E == 64) {
+#pragma unroll
+            for (int i = 0; i < 16; ++i)
+              reinterpret_cast<float4*>(lrow)[i] =
+                  make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+          } else {
+#pragma unroll
+            for (int i = 0; i < 64; ++i)
+              if (i < E) lrow[i] = v[i];
+          }
+        }
+#pragma unroll
+        for (int i = 0; i < 64; ++i)
+          if (i < E) mx = fmaxf(mx, v[i]);
+#pragma unroll
+        for (int i = 0; i < 64; ++i)
+          if (i < E) sum += expf(v[i] - mx);
+        // top-k by k selection passes over the 64 registers (the largest
+        // untaken value, ties to the lower index): far fewer instructions than
+        // an insertion list for k <= 8
+        uint64_t taken = 0;
+        for (int j = 0; j < k; ++j) {
+          float best = -INFINITY;
+          int b = -1;
+#pragma unroll
+          for (int i = 0; i < 64; ++i) {
+            const bool free_i = i < E && ((taken >> i) & 1ull) == 0;
+            if (free_i && (b < 0 || v[i] > best)) {
+              best = v[i];
+              b = i;
+            }
+          }
+          taken |= 1ull << b;
+          if (row_ok) {
+            p.topk_idx[static_cast<long long>(row) * k + j] = b;
+            p.topk_w[static_cast<long long>(row) * k + j] = expf(best - mx) / sum;
+          }
+        }
+      } else {
+        // pass 1: logits, max, top-k (insertion list), 32 columns at a time
+#pragma unroll 1
+        for (int sl = 0; sl < BN / 32; ++sl) {
+          float v[32];
+          {
+            uint32_t r[32];
+            tmem_ld32(t_row + sl * 32, r);
+            tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+          }
 #pragma unroll
           for (int i = 0; i < 32; ++i) {
             const int e = sl * 32 + i;
             if (e < E) {
-              lrow[e] = v[i];
+              if (row_ok) lrow[e] = v[i];
               mx = fmaxf(mx, v[i]);
               topk_insert(bv, bi, n, k, v[i], e);
             }
           }
         }
-      }
-      // pass 2: softmax denominator in ascending expert order
-      float sum = 0.f;
+        // pass 2: softmax denominator in ascending expert order
 #pragma unroll 1
-      for (int sl = 0; sl < BN / 32; ++sl) {
-        float v[32];
-        {
-          uint32_t r[32];
-          tmem_ld32(t_row + sl * 32, r);
-          tmem_wait_ld();
+        for (int sl = 0; sl < BN / 32; ++sl) {
+          float v[32];
+          {
+            uint32_t r[32];
+            tmem_ld32(t_row + sl * 32, r);
+            tmem_wait_ld();
 #pragma unroll
-          for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+            for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+          }
+#pragma unroll
+          for (int i = 0; i < 32; ++i)
+            if (sl * 32 + i < E) sum += expf(v[i] - mx);
         }
-#pragma unroll 1
-        for (int c = 1; c < nch; ++c) {
-          uint32_t r[32];
-          tmem_ld32(t_row + c * BN + sl * 32, r);
-          tmem_wait_ld();
-#pragma unroll
-          for (int i = 0; i < 32; ++i) v[i] += __uint_as_float(r[i]);
-        }
-#pragma unroll
-        for (int i = 0; i < 32; ++i)
-          if (sl * 32 + i < E) sum += expf(v[i] - mx);
       }
-      if (row_ok) {
+      if (BN > 64 && row_ok) {
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
           if (j < k) {

@@ -220,21 +220,31 @@ class ExpertParallelMoE:
     Buffers that peers touch (receive rows, expert outputs, count matrix,
     flags) are allocated with kvm_sm100_ipc_alloc and mapped into every rank
     through CUDA IPC handles exchanged over the process group once, at
-    construction. A call launches 11 or 12 kernels (LAUNCHES_PER_CALL) on the
-    current stream and never synchronises with the host: route, permute (local), count exchange,
+    construction. A call never synchronises with the host. Weak scaling: each
+    rank brings `max_tokens` tokens at most.
+
+    overlap=True (default): the all-to-all rides inside the grouped GEMMs --
+    route, permute, prepare (count exchange), local scatter, dispatch fused
+    with the gate/up GEMM (peer stores by extra warps; a local expert's tiles
+    start once every rank's rows for it have arrived), down GEMM whose
+    epilogue stores each result row straight back to the rank that routed the
+    token, wait for every rank's outputs, local combine: 9 or 10 launches.
+    overlap=False: the serial exchange -- route, permute, count exchange,
     dispatch (peer stores), wait, grouped GEMMs, signal, wait, combine (peer
-    loads). Weak scaling: each rank brings `max_tokens` tokens at most.
+    loads): 11 or 12 launches. Both are bit-identical to the one-GPU layer.
     """
 
     @property
     def LAUNCHES_PER_CALL(self) -> int:
-        """route 1, permute 2 or 3, count exchange 1, dispatch 1, wait 1,
-        grouped GEMMs 2, signal 1, wait 1, combine 1."""
+        """route 1, permute 2 or 3, then 6 (overlapped: prepare, local
+        scatter, dispatch + gate/up, down + push, wait, combine) or 8 (serial:
+        count exchange, dispatch, wait, grouped GEMMs 2, signal, wait,
+        combine)."""
         from .moe import permute_launches
-        return 9 + permute_launches(self.max_tokens * self.k, self.E)
+        return (7 if self.overlap else 9) + permute_launches(self.max_tokens * self.k, self.E)
 
     def __init__(self, w_router, w13, w2, *, top_k: int, max_tokens: int, rank: int,
-                 world: int, group=None):
+                 world: int, group=None, overlap: bool = True):
         import ctypes as C
         from ._lib import EpPeers, call, lib
         E, H = w_router.shape
@@ -267,8 +277,14 @@ class ExpertParallelMoE:
         self.done = torch.zeros(1, dtype=i32, device=dev)
         self.h = torch.empty((self.cap, self.F), dtype=torch.bfloat16, device=dev)
         self.out = torch.empty((T, H), dtype=torch.bfloat16, device=dev)
+        self.overlap = overlap
+        self.PHASES = self.PHASES_OVERLAP if overlap else self.PHASES_SERIAL
+        wsb = int(lib().kvm_sm100_ep_overlap_workspace(E, self.cap))
+        self.ws_ep = torch.empty(max(wsb, 256), dtype=torch.uint8, device=dev)
+        # flag words: counts, data, outputs ([world] each), then one per
+        # (local expert, source rank)
         sizes = {"recv": self.cap * H * 2, "y": self.cap * H * 2,
-                 "cnt": world * E * 4, "flags": 3 * world * 4}
+                 "cnt": world * E * 4, "flags": (3 * world + self.epr * world) * 4}
         self._own = {}
         for name, nbytes in sizes.items():
             p = C.c_void_p()
@@ -306,8 +322,11 @@ class ExpertParallelMoE:
             dist.barrier(group=group)
 
     # phase marks of a call (kvm_b200.timing.PhaseProbe): one per launch
-    PHASES = ["start", "router", "permute", "ep_counts", "ep_dispatch", "ep_wait_data",
-              "gate_up", "down", "ep_signal", "ep_wait_outputs", "ep_combine"]
+    PHASES_SERIAL = ["start", "router", "permute", "ep_counts", "ep_dispatch",
+                     "ep_wait_data", "gate_up", "down", "ep_signal", "ep_wait_outputs",
+                     "ep_combine"]
+    PHASES_OVERLAP = ["start", "router", "permute", "ep_prepare", "ep_scatter_local",
+                      "ep_dispatch_gate_up", "ep_down_push", "ep_wait_outputs", "combine"]
 
     def __call__(self, x, probe=None, out=None):
         from ._lib import call
@@ -331,6 +350,8 @@ class ExpertParallelMoE:
         call("kvm_sm100_moe_permute", self.idx.data_ptr(), T, k, E, self.offsets.data_ptr(),
              self.pos.data_ptr(), self.src.data_ptr(), self.ws.data_ptr(), st)
         mark("permute")
+        if self.overlap:
+            return self._overlapped(x, dst, ep, pr, st, mark)
         call("kvm_sm100_ep_counts", pr, self.offsets.data_ptr(), self.send_base.data_ptr(),
              self.loc_off.data_ptr(), ep, st)
         mark("ep_counts")
@@ -355,6 +376,31 @@ class ExpertParallelMoE:
              self.offsets.data_ptr(), self.send_base.data_ptr(), self.topw.data_ptr(),
              dst.data_ptr(), T, self.cap, st)
         mark("ep_combine")
+        return dst[:T]
+
+    def _overlapped(self, x, dst, ep, pr, st, mark):
+        from ._lib import call
+        T = x.shape[0]
+        H, F, k = self.H, self.F, self.k
+        ws = self.ws_ep.data_ptr()
+        call("kvm_sm100_ep_prepare", pr, self.offsets.data_ptr(), self.send_base.data_ptr(),
+             self.loc_off.data_ptr(), ws, self.cap, ep, st)
+        mark("ep_prepare")
+        call("kvm_sm100_ep_scatter_local", pr, x.data_ptr(), self.src.data_ptr(),
+             self.offsets.data_ptr(), self.send_base.data_ptr(), T, self.cap, st)
+        mark("ep_scatter_local")
+        call("kvm_sm100_ep_dispatch_gate_up", pr, x.data_ptr(), self.src.data_ptr(),
+             self.offsets.data_ptr(), self.send_base.data_ptr(), self.loc_off.data_ptr(),
+             self.w13.data_ptr(), self.h.data_ptr(), F, self.cap, ws, ep, st)
+        mark("ep_dispatch_gate_up")
+        call("kvm_sm100_ep_down_push", pr, self.h.data_ptr(), self.w2.data_ptr(),
+             self.loc_off.data_ptr(), F, self.cap, ws, ep, st)
+        mark("ep_down_push")
+        call("kvm_sm100_ep_wait", pr, 2, ep, st)
+        mark("ep_wait_outputs")
+        call("kvm_sm100_moe_combine", self._own["y"], self.pos.data_ptr(),
+             self.topw.data_ptr(), dst.data_ptr(), T, k, H, st)
+        mark("combine")
         return dst[:T]
 
     def close(self):

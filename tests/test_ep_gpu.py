@@ -32,7 +32,7 @@ def _tokens(rank, dev):
     return torch.randn((T, H), generator=g, device=dev).to(torch.bfloat16)
 
 
-def _worker(rank, world, port, outdir):
+def _worker(rank, world, port, outdir, overlap=True):
     import torch.distributed as dist
     from kvm_b200.ep import ExpertParallelMoE
     from kvm_b200 import ops
@@ -44,7 +44,8 @@ def _worker(rank, world, port, outdir):
                             timeout=timedelta(seconds=60), device_id=dev)
     try:
         wr, w13, w2 = _make(dev)
-        layer = ExpertParallelMoE(wr, w13, w2, top_k=K, max_tokens=T, rank=rank, world=world)
+        layer = ExpertParallelMoE(wr, w13, w2, top_k=K, max_tokens=T, rank=rank, world=world,
+                                  overlap=overlap)
         for _ in range(3):   # later calls reuse every buffer (epochs 2, 3)
             out = layer(_tokens(rank, dev))
         ops.device_status()
@@ -60,12 +61,13 @@ def _port():
         return s.getsockname()[1]
 
 
+@pytest.mark.parametrize("overlap", [True, False])
 @pytest.mark.parametrize("world", [2, 4, 8])
-def test_expert_parallel_matches_single_gpu(world):
+def test_expert_parallel_matches_single_gpu(world, overlap):
     if torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
     with tempfile.TemporaryDirectory() as d:
-        mp.start_processes(_worker, args=(world, _port(), d), nprocs=world,
+        mp.start_processes(_worker, args=(world, _port(), d, overlap), nprocs=world,
                            start_method="spawn")
         outs = [torch.load(os.path.join(d, f"out{r}.pt")) for r in range(world)]
     from kvm_b200.moe import MoELayer
@@ -77,16 +79,19 @@ def test_expert_parallel_matches_single_gpu(world):
     assert torch.equal(got.view(torch.int16), ref.view(torch.int16))
 
 
-def test_expert_parallel_single_rank_matches_layer(cuda):
-    """world = 1 runs every exchange kernel (flags, counts, dispatch, combine)
-    on one GPU; no kernel waits on a concurrently running one."""
+@pytest.mark.parametrize("overlap", [True, False])
+def test_expert_parallel_single_rank_matches_layer(cuda, overlap):
+    """world = 1 runs every exchange kernel (flags, counts, dispatch, combine;
+    overlapped: prepare, local scatter, the fused dispatch + gate/up and down
+    + push GEMMs) on one GPU; no kernel waits on a concurrently running one."""
     from kvm_b200.ep import ExpertParallelMoE
     from kvm_b200.moe import MoELayer
     from kvm_b200 import ops
     wr, w13, w2 = _make(cuda)
     x = _tokens(0, cuda)
     ref = MoELayer(wr, w13, w2, K, T)(x).clone()
-    layer = ExpertParallelMoE(wr, w13, w2, top_k=K, max_tokens=T, rank=0, world=1)
+    layer = ExpertParallelMoE(wr, w13, w2, top_k=K, max_tokens=T, rank=0, world=1,
+                              overlap=overlap)
     for _ in range(3):
         out = layer(x)
     ops.device_status()

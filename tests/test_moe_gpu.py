@@ -50,9 +50,8 @@ def test_router_topk_bit_exact_given_logits(cuda, T, k, E):
 @pytest.mark.parametrize("H", [4096, 200, 64])
 def test_router_logits_do_not_depend_on_the_batch(cuda, H):
     """A token's logits are the same bits whichever batch (and so tile and
-    CTA) it is routed in: the expert-parallel layer relies on it. H = 4096
-    splits K into 8 chunks walked from different starting chunks by different
-    CTAs; H = 200 ends in a partial K block; H = 64 is one chunk."""
+    CTA) it is routed in: the expert-parallel layer relies on it. H = 200
+    ends in a partial K block; H = 64 is a single one."""
     rng = np.random.default_rng(H)
     T, E, k = 8192, 64, 2
     x = from_bits(oracle.normal_bf16(rng, (T, H)), cuda)
