@@ -301,6 +301,22 @@ __global__ void ep_prepare_kernel(const kvm_ep_peers pr, const int* __restrict__
     }
     ws.seg_prefix[nseg] = q;
   }
+  // token tile (of the fused gate/up GEMM's split of each local expert's rows
+  // into ceil(rows / 256) tiles of equal width rounded up to 16) that holds
+  // this rank's own rows: the GEMM starts each expert there
+  for (int le = threadIdx.x; le < epr; le += blockDim.x) {
+    const int e = me * epr + le;
+    const int c = tot[e];
+    const int tt = (c + 255) / 256;
+    int first = 0;
+    if (tt >= 2) {
+      const int tn = ((c + tt - 1) / tt + 15) & ~15;
+      int before = 0;
+      for (int r = 0; r < me; ++r) before += cnt[r * E + e];
+      first = min(tt - 1, before / tn);
+    }
+    ws.tile_first[le] = first;
+  }
   // where this rank's rows of expert e start in the owner's receive buffer:
   // after the owner's earlier local experts, then after lower source ranks
   for (int e = threadIdx.x; e < E; e += blockDim.x) {

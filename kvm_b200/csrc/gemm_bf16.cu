@@ -412,6 +412,7 @@ int ep_common(const kvm_ep_peers* pr, int64_t cap_rows, const void* workspace,
   ep->seg_prefix = ws.seg_prefix;
   ep->nseg = ep->epr * (pr->world - 1);
   ep->push_row = ws.push_row;
+  ep->tile_first = ws.tile_first;
   ep->done_ctr = ws.done_ctr;
   return KVM_OK;
 }

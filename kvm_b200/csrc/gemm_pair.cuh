@@ -121,6 +121,7 @@ struct PairEp {
   // kEpDownPush
   void* push_base[8];             // every rank's result rows [T*k, H]
   const int* push_row;            // [rows] (source rank << 28) | row there
+  const int* tile_first;          // [epr] first token tile of each group
   int* done_ctr;                  // CTAs finished (zero at launch)
 };
 
@@ -131,22 +132,24 @@ __device__ __forceinline__ unsigned* ep_group_flag(const PairEp& ep, int owner, 
   return ep.flags[owner] + 3 * ep.P + le * ep.P + src;
 }
 
-// Bounded wait until every other rank's flag for group g holds this epoch,
-// then order the TMA loads that follow after those acquires.
-__device__ __forceinline__ bool ep_wait_group(const PairEp& ep, int g,
-                                              volatile int* abort) {
+// Bounded wait until the flags for group g of the ranks in `mask` hold this
+// epoch (acquire loads), then order the TMA loads that follow after them.
+// (Polling them all as relaxed loads followed by one fence.acq_rel.sys was
+// measured 27% slower for the whole kernel on 2 GPUs: that fence is costly.)
+__device__ __forceinline__ bool ep_wait_sources(const PairEp& ep, int g, unsigned mask,
+                                                volatile int* abort) {
+  const unsigned* f = ep_group_flag(ep, ep.me, g, 0);
   for (int s = 0; s < ep.P; ++s) {
-    if (s == ep.me) continue;
-    const unsigned* f = ep_group_flag(ep, ep.me, g, s);
-    if (ld_acquire_sys(f) >= ep.epoch) continue;
+    if (!((mask >> s) & 1u)) continue;
+    if (ld_acquire_sys(f + s) >= ep.epoch) continue;
     const uint64_t t0 = globaltimer_ns();
-    while (ld_acquire_sys(f) < ep.epoch) {
+    while (ld_acquire_sys(f + s) < ep.epoch) {
       if (*abort) return false;
       if (globaltimer_ns() - t0 > kWaitTimeoutNs) {
         *abort = 1;
         return false;
       }
-      __nanosleep(128);
+      __nanosleep(64);
     }
   }
   fence_proxy_async_global();
@@ -231,7 +234,7 @@ __device__ void ep_dispatch_rows(const PairEp& ep, int w, int nw, int lane) {
 constexpr size_t gemm_pair_smem_bytes() {
   return 1024 + static_cast<size_t>(kPairStages) * kPairStageBytes +
          kPairUBytes + (2 * kPairStages + 2 + 2 + 1 + 4) * 8 + 16 +
-         4 * (kMaxGroups + 1) * 4;
+         5 * (kMaxGroups + 1) * 4;
 }
 
 // SiLU(g) = g * sigmoid(g) with the fast reciprocal-based divide; the
@@ -275,6 +278,7 @@ __global__ void __launch_bounds__(pair_threads(EP), 1)
   int* g_pref = g_off + (kMaxGroups + 1);              // [G+1] tile prefix
   int* g_tt = g_pref + (kMaxGroups + 1);               // [G] token tiles
   int* g_tn = g_tt + (kMaxGroups + 1);                 // [G] token tile width
+  int* g_tme = g_tn + (kMaxGroups + 1);                // [G] first token tile in order
 
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
@@ -285,8 +289,10 @@ __global__ void __launch_bounds__(pair_threads(EP), 1)
 
   // ---- setup: tile table (identical in both CTAs), barriers, TMEM
   if (threadIdx.x == 0) *abort_flag = 0;
-  for (int i = threadIdx.x; i <= G; i += blockDim.x)
+  for (int i = threadIdx.x; i <= G; i += blockDim.x) {
     g_off[i] = p.offsets ? p.offsets[i] : (i == 0 ? 0 : p.rows);
+    if (EP == kEpDispatchGateUp && i < G) g_tme[i] = ep.tile_first[i];
+  }
   __syncthreads();
   if (threadIdx.x == 0) {
     int acc = 0;
@@ -306,6 +312,14 @@ __global__ void __launch_bounds__(pair_threads(EP), 1)
     }
     g_pref[G] = acc;
     if (bad && p.status && cr == 0) atomicOr(p.status, kDevBadInput);
+    // Expert-parallel gate/up: a group's rows are source-rank-major, and the
+    // rows of source me - 1 arrive first, then me - 2, ... (every rank sends
+    // its segments to me + 1, me + 2, ... in that order). Token tiles run in
+    // that order too: first the tile holding this rank's own rows (already
+    // here; its index comes with the call's workspace), then downwards,
+    // wrapping around.
+    for (int g = 0; g < G; ++g)
+      g_tme[g] = EP == kEpDispatchGateUp ? min(max(g_tme[g], 0), max(g_tt[g] - 1, 0)) : 0;
     for (int s = 0; s < kPairStages; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
@@ -348,7 +362,8 @@ __global__ void __launch_bounds__(pair_threads(EP), 1)
     const int local = t - g_pref[lo];
     const int tt = g_tt[lo];
     tl.mi = local / tt;
-    const int ti = local - tl.mi * tt;
+    int ti = local - tl.mi * tt;
+    if constexpr (EP == kEpDispatchGateUp) ti = (g_tme[lo] - ti + tt) % tt;
     const int tnb = g_tn[lo];
     tl.r0 = g_off[lo] + ti * tnb;
     tl.valid = min(tnb, g_off[lo + 1] - tl.r0);
@@ -363,13 +378,22 @@ __global__ void __launch_bounds__(pair_threads(EP), 1)
       int s = 0;
       uint32_t ph = 0;
       bool ok = true;
-      int ready_g = -1;  // groups whose rows from every rank have arrived
+      int ready_g = -1;           // group of ready_mask
+      unsigned ready_mask = 0;    // ranks whose rows of group ready_g have arrived
       for (int t = cl0; t < total_tiles && ok; t += ncl) {
         const PairTile tl = map_tile(t);
         if constexpr (EP == kEpDispatchGateUp) {
-          if (tl.g > ready_g) {
-            if (!ep_wait_group(ep, tl.g, abort_flag)) { ok = false; break; }
+          // wait only for the ranks whose rows this tile holds
+          if (tl.g != ready_g) {
             ready_g = tl.g;
+            ready_mask = 1u << ep.me;
+          }
+          const int s_lo = __ldg(ep.push_row + tl.r0) >> 28;
+          const int s_hi = __ldg(ep.push_row + tl.r0 + tl.valid - 1) >> 28;
+          const unsigned need = ((2u << s_hi) - (1u << s_lo)) & ~ready_mask;
+          if (need) {
+            if (!ep_wait_sources(ep, tl.g, need, abort_flag)) { ok = false; break; }
+            ready_mask |= need;
           }
         }
         // rows this CTA stages: the smallest box covering tn/2 token rows
