@@ -104,6 +104,19 @@ struct Executor::Routing {
   int32_t* pos = nullptr;
   int32_t* src = nullptr;
   void* ws = nullptr;
+  // Expert parallelism over the op's ranks (P > 1): this rank (position me in
+  // the rank set) owns experts [me*epr, (me+1)*epr); rows routed to them from
+  // every rank arrive in `recv` (cap = T*k*P rows), expert outputs go to `y`;
+  // both are mapped into every member (CUDA IPC).
+  int P = 1, me = 0, epr = 0;
+  int64_t cap = 0;
+  kvm_ep_peers peers{};
+  int32_t* send_base = nullptr;
+  int32_t* loc_off = nullptr;
+  uint32_t* done = nullptr;
+  uint32_t epoch = 0;  // per Run, the same on every member
+  kvm_comm* comm = nullptr;
+  std::vector<void*> own_ipc, opened_ipc;
 };
 
 struct Executor::Slot {
@@ -149,6 +162,26 @@ Executor::Executor(const ir::Graph& kernel, const ir::AttrMap& attrs)
 }
 
 Executor::~Executor() {
+  // Expert-parallel peer memory: every member stops using the others' buffers
+  // (a barrier over the group's communicator) before any of them is freed.
+  bool any_ep = false;
+  for (auto& r : routings_) any_ep = any_ep || !r->own_ipc.empty();
+  if (any_ep) {
+    cudaDeviceSynchronize();
+    void* one = nullptr;
+    if (cudaMalloc(&one, sizeof(float)) == cudaSuccess) {
+      for (auto& r : routings_) {
+        if (r->own_ipc.empty()) continue;
+        kvm_sm100_all_reduce(r->comm, one, one, 1, KVM_EW_F32, KVM_RED_SUM, nullptr);
+        cudaDeviceSynchronize();
+        for (void* q : r->opened_ipc) kvm_sm100_ipc_close(q);
+        kvm_sm100_all_reduce(r->comm, one, one, 1, KVM_EW_F32, KVM_RED_SUM, nullptr);
+        cudaDeviceSynchronize();
+        for (void* q : r->own_ipc) kvm_sm100_ipc_free(q);
+      }
+      cudaFree(one);
+    }
+  }
   for (auto& kv : subcomms_)
     if (kv.second && kv.second != world_) kvm_sm100_comm_destroy(kv.second);
   for (void* p : allocations_) cudaFree(p);
@@ -556,10 +589,19 @@ void Executor::PlanSilu(const ir::ValueNode* dst) {
   Routing* r = slot(BaseGlobal(mg.args[0])).group;
   if (Wg.shape.size() == 3) {
     if (!r || r->E != E) Fail("per-expert SiLU-gate GEMM needs A grouped by a moe_dispatch");
-    steps_.push_back([=](cudaStream_t st) {
-      return kvm_sm100_grouped_gemm_bf16(a, w13, d, r->offsets, int(E), int(M),
-                                         int(2 * F), int(K), 2, st);
-    });
+    if (r->P > 1) {
+      if (M != r->cap) Fail("expert-parallel GEMM rows must be the dispatch's T*top_k*ranks");
+      const void* wl = static_cast<const char*>(w13) + int64_t(r->me) * r->epr * 2 * F * K * 2;
+      steps_.push_back([=](cudaStream_t st) {
+        return kvm_sm100_grouped_gemm_bf16(a, wl, d, r->loc_off, r->epr, int(M),
+                                           int(2 * F), int(K), 2, st);
+      });
+    } else {
+      steps_.push_back([=](cudaStream_t st) {
+        return kvm_sm100_grouped_gemm_bf16(a, w13, d, r->offsets, int(E), int(M),
+                                           int(2 * F), int(K), 2, st);
+      });
+    }
     step_names_.push_back("grouped_gemm_silu_gate");
   } else {
     steps_.push_back([=](cudaStream_t st) {
@@ -662,6 +704,17 @@ void Executor::PlanGemm(const ir::ValueNode* mma, const Buffer& out) {
   Routing* r = s.group;
   const void* a = A.ptr;
   void* d = out.ptr;
+  if (r->P > 1) {
+    // this rank's experts over the rows it received
+    if (M != r->cap) Fail("expert-parallel GEMM rows must be the dispatch's T*top_k*ranks");
+    const void* bl = static_cast<const char*>(bt) + int64_t(r->me) * r->epr * N * K * 2;
+    steps_.push_back([=](cudaStream_t st) {
+      return kvm_sm100_grouped_gemm_bf16(a, bl, d, r->loc_off, r->epr, int(M), int(N),
+                                         int(K), 0, st);
+    });
+    step_names_.push_back("grouped_gemm_bf16");
+    return;
+  }
   steps_.push_back([=](cudaStream_t st) {
     return kvm_sm100_grouped_gemm_bf16(a, bt, d, r->offsets, int(E), int(M), int(N),
                                        int(K), 0, st);
@@ -762,6 +815,178 @@ void Executor::PlanExpr(const ir::ValueNode* expr, const Buffer& out) {
   step_names_.push_back("elementwise");
 }
 
+// Routing of a moe_dispatch (one rank or several): top_k from the kernel op's
+// attrs, then softmax + top-k (fused with the router GEMM when its logits feed
+// only the MoE ops) and the expert-major permutation of this rank's pairs.
+Executor::Routing* Executor::PlanRoute(const ir::OpNode* op, const ir::OpNode* kop,
+                                       const Buffer& x, const Buffer& g) {
+  if (x.shape.size() != 2 || g.shape.size() != 2 || g.shape[0] != x.shape[0])
+    Fail("moe_dispatch(x [T,H], g [T,E]) shapes disagree");
+  if (x.dtype != Dtype::kBf16) Fail("moe_dispatch tokens must be bf16");
+  int k = 2;
+  if (kop)
+    if (const std::any* a = attrs_.Get(kop, "top_k"))
+      if (const auto* v = std::any_cast<std::int64_t>(a)) k = int(*v);
+  Routing* r = routing_by_op_.at(op);
+  r->T = int(x.shape[0]);
+  r->E = int(g.shape[1]);
+  r->k = k;
+  const int64_t n = int64_t(r->T) * k;
+  r->idx = static_cast<int32_t*>(Alloc(n * 4));
+  r->w = static_cast<float*>(Alloc(n * 4));
+  r->offsets = static_cast<int32_t*>(Alloc((r->E + 1) * 4));
+  r->pos = static_cast<int32_t*>(Alloc(n * 4));
+  r->src = static_cast<int32_t*>(Alloc(n * 4));
+  r->ws = Alloc(kvm_sm100_moe_permute_workspace(r->T, k, r->E));
+  Routing* rp = r;
+  void* gp = g.ptr;
+  const int gd = EwDtype(g.dtype);
+  auto rt = router_.find(BaseGlobal(op->operands()[1]));
+  if (rt != router_.end()) {
+    // router GEMM + softmax + top-k in one kernel; its weight [H, E] is
+    // re-laid out once to [E, H]
+    const Buffer& ra = GlobalOf(rt->second.first);
+    const Buffer& rw = GlobalOf(rt->second.second);
+    const int RH = int(rw.shape[0]), RE = int(rw.shape[1]);
+    void* wt = Alloc(rw.bytes());
+    const void* wsrc = rw.ptr;
+    once_steps_.push_back([=](cudaStream_t st) {
+      return kvm_sm100_transpose_bf16(wsrc, wt, 1, RH, RE, st);
+    });
+    const void* ap = ra.ptr;
+    steps_.push_back([=](cudaStream_t st) {
+      return kvm_sm100_moe_router_topk(ap, wt, static_cast<float*>(gp), rp->idx, rp->w,
+                                       rp->T, RH, RE, rp->k, st);
+    });
+    step_names_.push_back("moe_router_topk");
+  } else {
+    steps_.push_back([=](cudaStream_t st) {
+      return kvm_sm100_moe_topk(gp, gd, rp->T, rp->E, rp->k, rp->idx, rp->w, st);
+    });
+    step_names_.push_back("moe_topk");
+  }
+  steps_.push_back([=](cudaStream_t st) {
+    return kvm_sm100_moe_permute(rp->idx, rp->T, rp->k, rp->E, rp->offsets, rp->pos,
+                                 rp->src, rp->ws, st);
+  });
+  step_names_.push_back("moe_permute");
+  return r;
+}
+
+// moe_dispatch over several ranks: expert parallelism. The rank set's
+// communicator carries a one-time exchange of CUDA IPC handles (receive rows,
+// expert outputs, count matrix, flags) at Prepare; every Run then routes and
+// permutes this rank's tokens, exchanges counts, stores each routed row into
+// its owner's receive buffer (peer stores) and waits for every member's rows.
+// The dispatch result is the receive buffer: T*top_k*ranks rows (capacity),
+// expert-major then source-rank-major, of which the first loc_off[E/ranks]
+// are filled; the expert GEMMs over it use this rank's experts only.
+void Executor::PlanExpertDispatch(const ir::OpNode* op, const std::vector<int>& ranks) {
+  int nth = 0;
+  for (const ir::OpNode* o : task_.root()->operations()) {
+    if (o == op) break;
+    if (o->op().op.name == "comm.moe_dispatch") ++nth;
+  }
+  const ir::OpNode* kop = KernelCommOp("comm.moe_dispatch", nth);
+  const ir::ValueNode* res = op->results()[0];
+  if (!world_)
+    Fail("moe_dispatch over " + std::to_string(ranks.size()) +
+         " ranks needs a communicator (kvm_run --rank/--world)");
+  if (ranks.size() > KVM_EP_MAX_RANKS) Fail("expert parallelism over more than 8 ranks");
+  int me = -1;
+  kvm_comm* comm = CommFor(ranks, &me);
+  if (me < 0) Fail("this rank is not in the moe_dispatch's rank set");
+  const Buffer x = GlobalOf(op->operands()[0]);
+  const Buffer g = GlobalOf(op->operands()[1]);
+  Routing* r = PlanRoute(op, kop, x, g);
+  const int P = int(ranks.size()), E = r->E, H = int(x.shape[1]);
+  if (E % P != 0) Fail("moe_dispatch: the experts must split evenly over the ranks");
+  r->P = P;
+  r->me = me;
+  r->epr = E / P;
+  r->comm = comm;
+  r->cap = int64_t(r->T) * r->k * P;
+  // peer buffers, mapped into every member
+  const int64_t bytes[4] = {r->cap * H * 2, r->cap * H * 2, int64_t(P) * E * 4,
+                            int64_t(3 + r->epr) * P * 4};
+  void* own[4];
+  for (int i = 0; i < 4; ++i) {
+    if (kvm_sm100_ipc_alloc(bytes[i], &own[i]) != KVM_OK)
+      Fail(std::string("expert parallel: ") + kvm_sm100_last_error());
+    r->own_ipc.push_back(own[i]);
+  }
+  std::vector<char> mine(4 * 64), all(size_t(P) * 4 * 64);
+  for (int i = 0; i < 4; ++i)
+    if (kvm_sm100_ipc_get_handle(own[i], mine.data() + i * 64) != KVM_OK)
+      Fail(std::string("expert parallel: ") + kvm_sm100_last_error());
+  void* dev = Alloc(int64_t(P + 1) * 4 * 64);
+  void* dev_all = static_cast<char*>(dev) + 4 * 64;
+  cudaMemcpy(dev, mine.data(), mine.size(), cudaMemcpyHostToDevice);
+  if (kvm_sm100_all_gather(comm, dev, dev_all, 4 * 64 / 4, KVM_EW_I32, nullptr) != KVM_OK)
+    Fail(std::string("expert parallel: handle exchange: ") + kvm_sm100_last_error());
+  cudaDeviceSynchronize();
+  cudaMemcpy(all.data(), dev_all, all.size(), cudaMemcpyDeviceToHost);
+  kvm_ep_peers& pr = r->peers;
+  std::memset(&pr, 0, sizeof(pr));
+  pr.rank = me;
+  pr.world = P;
+  pr.E = E;
+  pr.H = H;
+  pr.k = r->k;
+  for (int q = 0; q < P; ++q) {
+    void* ptr[4];
+    for (int i = 0; i < 4; ++i) {
+      if (q == me) {
+        ptr[i] = own[i];
+      } else {
+        if (kvm_sm100_ipc_open_handle(all.data() + (size_t(q) * 4 + i) * 64, &ptr[i]) !=
+            KVM_OK)
+          Fail(std::string("expert parallel: ") + kvm_sm100_last_error());
+        r->opened_ipc.push_back(ptr[i]);
+      }
+    }
+    pr.recv[q] = ptr[0];
+    pr.y[q] = ptr[1];
+    pr.cnt[q] = ptr[2];
+    pr.flags[q] = ptr[3];
+  }
+  r->send_base = static_cast<int32_t*>(Alloc(int64_t(E) * 4));
+  r->loc_off = static_cast<int32_t*>(Alloc(int64_t(r->epr + 1) * 4));
+  r->done = static_cast<uint32_t*>(Alloc(16));
+  cudaMemset(r->done, 0, 16);
+  // the dispatch result lives in the receive buffer; the expert outputs the
+  // matching moe_combine reads live in the peer-visible y buffer
+  Slot& rs = slot(res);
+  if (rs.buf.numel() != r->cap * H || rs.buf.dtype != Dtype::kBf16)
+    Fail("moe_dispatch over " + std::to_string(P) + " ranks: result must be bf16 [T*top_k*" +
+         std::to_string(P) + ", H] (this rank's receive capacity)");
+  rs.buf.ptr = own[0];
+  for (const ir::OpNode* c : consumers_[BaseGlobal(op->operands()[1])])
+    if (c->op().op.name == "comm.moe_combine") {
+      Slot& ys = slot(BaseGlobal(c->operands()[0]));
+      if (!ys.buf.ptr && ys.buf.numel() == r->cap * H && ys.buf.dtype == Dtype::kBf16)
+        ys.buf.ptr = own[1];
+    }
+  Routing* rp = r;
+  const kvm_ep_peers* prp = &r->peers;
+  const void* xp = x.ptr;
+  steps_.push_back([=](cudaStream_t st) {
+    ++rp->epoch;
+    return kvm_sm100_ep_counts(prp, rp->offsets, rp->send_base, rp->loc_off, rp->epoch, st);
+  });
+  step_names_.push_back("ep_counts");
+  steps_.push_back([=](cudaStream_t st) {
+    return kvm_sm100_ep_dispatch(prp, xp, rp->idx, rp->pos, rp->offsets, rp->send_base,
+                                 rp->T, rp->cap, rp->done, rp->epoch, st);
+  });
+  step_names_.push_back("ep_dispatch");
+  steps_.push_back([=](cudaStream_t st) {
+    return kvm_sm100_ep_wait(prp, 1, rp->epoch, st);
+  });
+  step_names_.push_back("ep_wait");
+  routing_of_[g.ptr] = r;
+}
+
 void Executor::PlanComm(const ir::OpNode* op) {
   const std::string name = op->op().op.name;  // "comm.moe_dispatch", ...
   int nth = 0;
@@ -771,78 +996,31 @@ void Executor::PlanComm(const ir::OpNode* op) {
   }
   const ir::OpNode* kop = KernelCommOp(name, nth);
   const ir::ValueNode* res = op->results()[0];
+  std::vector<int> moe_ranks;
   if (name == "comm.moe_dispatch" || name == "comm.moe_combine") {
-    // Expert parallelism across ranks (tokens exchanged between the experts'
-    // owners) is the Python layer kvm_b200.ep; a graph op over one rank runs
-    // here. Anything else fails rather than silently computing one rank's part.
-    std::vector<int> ranks;
-    if (const auto* r = op->op().impl.as<ir::kernel::MoeDispatch>()) ranks = r->ranks;
-    if (const auto* r = op->op().impl.as<ir::kernel::MoeCombine>()) ranks = r->ranks;
-    std::sort(ranks.begin(), ranks.end());
-    ranks.erase(std::unique(ranks.begin(), ranks.end()), ranks.end());
-    if (ranks.size() > 1)
-      Fail("'" + name + "' over " + std::to_string(ranks.size()) +
-           " ranks: expert parallelism runs through kvm_b200.ep, not the graph executor");
+    // Over several ranks the op is the expert-parallel exchange: the experts
+    // are split evenly over the ranks (in the order of the op's rank list),
+    // and the exchange runs over NVLink peer memory (ep.cu).
+    if (const auto* r = op->op().impl.as<ir::kernel::MoeDispatch>()) moe_ranks = r->ranks;
+    if (const auto* r = op->op().impl.as<ir::kernel::MoeCombine>()) moe_ranks = r->ranks;
+    std::sort(moe_ranks.begin(), moe_ranks.end());
+    moe_ranks.erase(std::unique(moe_ranks.begin(), moe_ranks.end()), moe_ranks.end());
+  }
+  if (name == "comm.moe_dispatch" && moe_ranks.size() > 1) {
+    PlanExpertDispatch(op, moe_ranks);
+    return;
   }
   if (name == "comm.moe_dispatch") {
     const Buffer x = GlobalOf(op->operands()[0]);
     const Buffer g = GlobalOf(op->operands()[1]);
-    if (x.shape.size() != 2 || g.shape.size() != 2 || g.shape[0] != x.shape[0])
-      Fail("moe_dispatch(x [T,H], g [T,E]) shapes disagree");
-    if (x.dtype != Dtype::kBf16) Fail("moe_dispatch tokens must be bf16");
-    int k = 2;
-    if (kop)
-      if (const std::any* a = attrs_.Get(kop, "top_k"))
-        if (const auto* v = std::any_cast<std::int64_t>(a)) k = int(*v);
-    Routing* r = routing_by_op_.at(op);
-    r->T = int(x.shape[0]);
-    r->E = int(g.shape[1]);
-    r->k = k;
-    const int64_t n = int64_t(r->T) * k;
-    r->idx = static_cast<int32_t*>(Alloc(n * 4));
-    r->w = static_cast<float*>(Alloc(n * 4));
-    r->offsets = static_cast<int32_t*>(Alloc((r->E + 1) * 4));
-    r->pos = static_cast<int32_t*>(Alloc(n * 4));
-    r->src = static_cast<int32_t*>(Alloc(n * 4));
-    r->ws = Alloc(kvm_sm100_moe_permute_workspace(r->T, k, r->E));
+    Routing* rp = PlanRoute(op, kop, x, g);
+    const int64_t n = int64_t(rp->T) * rp->k;
     Buffer& out = Materialize(res);
     if (out.numel() != n * x.shape[1] || out.dtype != Dtype::kBf16)
       Fail("moe_dispatch result must be bf16 [T*top_k, H]");
-    Routing* rp = r;
-    void* gp = g.ptr;
-    const int gd = EwDtype(g.dtype);
     const void* xp = x.ptr;
     void* dp = out.ptr;
     const int H = int(x.shape[1]);
-    auto rt = router_.find(BaseGlobal(op->operands()[1]));
-    if (rt != router_.end()) {
-      // router GEMM + softmax + top-k in one kernel; its weight [H, E] is
-      // re-laid out once to [E, H]
-      const Buffer& ra = GlobalOf(rt->second.first);
-      const Buffer& rw = GlobalOf(rt->second.second);
-      const int RH = int(rw.shape[0]), RE = int(rw.shape[1]);
-      void* wt = Alloc(rw.bytes());
-      const void* wsrc = rw.ptr;
-      once_steps_.push_back([=](cudaStream_t st) {
-        return kvm_sm100_transpose_bf16(wsrc, wt, 1, RH, RE, st);
-      });
-      const void* ap = ra.ptr;
-      steps_.push_back([=](cudaStream_t st) {
-        return kvm_sm100_moe_router_topk(ap, wt, static_cast<float*>(gp), rp->idx, rp->w,
-                                         rp->T, RH, RE, rp->k, st);
-      });
-      step_names_.push_back("moe_router_topk");
-    } else {
-      steps_.push_back([=](cudaStream_t st) {
-        return kvm_sm100_moe_topk(gp, gd, rp->T, rp->E, rp->k, rp->idx, rp->w, st);
-      });
-      step_names_.push_back("moe_topk");
-    }
-    steps_.push_back([=](cudaStream_t st) {
-      return kvm_sm100_moe_permute(rp->idx, rp->T, rp->k, rp->E, rp->offsets, rp->pos,
-                                   rp->src, rp->ws, st);
-    });
-    step_names_.push_back("moe_permute");
     steps_.push_back([=](cudaStream_t st) {
       return kvm_sm100_moe_scatter_rows(xp, rp->pos, dp, rp->T, rp->k, H, st);
     });
@@ -860,6 +1038,32 @@ void Executor::PlanComm(const ir::OpNode* op) {
     const int H = int(y.shape.back());
     if (out.numel() != int64_t(rp->T) * H || out.dtype != Dtype::kBf16)
       Fail("moe_combine result must be bf16 [T, H]");
+    if ((moe_ranks.size() > 1) != (rp->P > 1))
+      Fail("moe_combine must run over the rank set of its moe_dispatch");
+    if (rp->P > 1) {
+      // The reverse exchange: every member's expert outputs are complete,
+      // then each token's k rows are loaded from their owners (peer loads)
+      // and combined as on one GPU.
+      if (y.ptr != rp->peers.y[rp->me] || y.numel() != rp->cap * H)
+        Fail("expert-parallel moe_combine(y, g): y must be the expert GEMM output over the "
+             "dispatch's rows [T*top_k*ranks, H]");
+      const kvm_ep_peers* pr = &rp->peers;
+      void* o = out.ptr;
+      steps_.push_back([=](cudaStream_t st) {
+        return kvm_sm100_ep_signal(pr, 2, rp->epoch, st);
+      });
+      step_names_.push_back("ep_signal");
+      steps_.push_back([=](cudaStream_t st) {
+        return kvm_sm100_ep_wait(pr, 2, rp->epoch, st);
+      });
+      step_names_.push_back("ep_wait");
+      steps_.push_back([=](cudaStream_t st) {
+        return kvm_sm100_ep_combine(pr, rp->idx, rp->pos, rp->offsets, rp->send_base, rp->w,
+                                    o, rp->T, rp->cap, st);
+      });
+      step_names_.push_back("ep_combine");
+      return;
+    }
     const void* yp = y.ptr;
     void* op_ = out.ptr;
     steps_.push_back([=](cudaStream_t st) {

@@ -107,6 +107,9 @@ class Executor {
   void PlanGemm(const ir::ValueNode* mma, const Buffer& out);
   void PlanExpr(const ir::ValueNode* expr, const Buffer& out);
   void PlanComm(const ir::OpNode* op);
+  void PlanExpertDispatch(const ir::OpNode* op, const std::vector<int>& ranks);
+  Routing* PlanRoute(const ir::OpNode* op, const ir::OpNode* kop, const Buffer& x,
+                     const Buffer& g);
   void PlanSilu(const ir::ValueNode* dst);
   void PlanRms(const ir::ValueNode* dst);
   void* Alloc(int64_t bytes);

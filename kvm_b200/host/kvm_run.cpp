@@ -20,7 +20,8 @@
 // GPU R): rank 0 writes the NCCL unique id to DIR/nccl_id (the others wait
 // for it, 60 s at most; DIR starts empty), the graph's comm.* ops run over NCCL, inputs come
 // from <inputs>/r<R>/ and outputs go to <out>/r<R>/, and seeded inputs
-// use seed S + 1000003 R + argument index.
+// use seed S + 1000003 R + argument index ({replicated = true} arguments, such
+// as expert weights, use seed S + argument index on every rank).
 #include <cuda_runtime.h>
 
 #include <any>
@@ -30,6 +31,7 @@
 #include <cstring>
 #include <fstream>
 #include <iostream>
+#include <memory>
 #include <sstream>
 #include <string>
 #include <vector>
@@ -204,12 +206,16 @@ int main(int argc, char** argv) {
       if (comm_dir.empty()) throw std::runtime_error("--world > 1 needs --comm-dir");
       comm = JoinWorld(rank, world, comm_dir);  // selects GPU `rank` first
     }
-    kvm::sm100::Executor ex(kernel, attrs);
+    // The executor holds peer memory of the other ranks (expert-parallel
+    // graphs) and releases it collectively, so it goes before the communicator.
+    auto exec = std::make_unique<kvm::sm100::Executor>(kernel, attrs);
+    kvm::sm100::Executor& ex = *exec;
+    uint64_t rank_seed = seed;
     if (comm) {
       ex.SetComm(comm);
       if (!in_dir.empty()) in_dir += "/r" + std::to_string(rank);
       if (!out_dir.empty()) out_dir += "/r" + std::to_string(rank);
-      seed += 1000003ull * uint64_t(rank);
+      rank_seed += 1000003ull * uint64_t(rank);
     }
     if (dump_task) {
       kvm::ir::serial::Registry treg;
@@ -265,16 +271,20 @@ int main(int argc, char** argv) {
     for (std::size_t i = 0; i < ex.inputs().size(); ++i) {
       const std::string& name = ex.input_names()[i];
       std::vector<char> data;
-      bool f_fill = false, f_std = false, f_mean = false;
+      bool f_fill = false, f_std = false, f_mean = false, f_rep = false;
       const double fill = AttrNumber(attrs, args[i], "fill", &f_fill);
       const double sd = AttrNumber(attrs, args[i], "std", &f_std);
       const double mean = AttrNumber(attrs, args[i], "mean", &f_mean);
+      const std::any* rep = attrs.Get(args[i], "replicated");
+      if (rep)
+        if (const bool* b = std::any_cast<bool>(rep)) f_rep = *b;
       if (!in_dir.empty() && ReadBin(in_dir + "/" + name + ".bin", data))
         ex.CopyInput(int(i), data.data(), int64_t(data.size()));
       else if (f_fill)
         ex.FillInputConst(int(i), float(fill));
-      else
-        ex.FillInputNormal(int(i), seed + i, float(mean), f_std ? float(sd) : 1.0f);
+      else  // {replicated = true}: the same values on every rank (e.g. weights)
+        ex.FillInputNormal(int(i), (f_rep ? seed : rank_seed) + i, float(mean),
+                           f_std ? float(sd) : 1.0f);
     }
     cudaStream_t st;
     cudaStreamCreate(&st);
@@ -327,6 +337,7 @@ int main(int argc, char** argv) {
     js << "]}";
     std::cout << js.str() << std::endl;
     cudaStreamDestroy(st);
+    exec.reset();
     if (comm) kvm_sm100_comm_destroy(comm);
   } catch (const std::exception& e) {
     std::cerr << "kvm_run: " << e.what() << std::endl;

@@ -137,9 +137,10 @@ def test_collectives_over_nccl(cuda, tmp_path, world):
 
 @pytest.mark.gpu
 def test_expert_parallel_graph_ops_fail_loudly(cuda, tmp_path):
-    """moe_dispatch over more than one rank is expert parallelism, which runs
-    through kvm_b200.ep; the graph executor refuses it instead of computing
-    one rank's share."""
+    """moe_dispatch over more than one rank is expert parallelism: run as a
+    single process (no communicator), the graph executor refuses it instead
+    of computing one rank's share (tests/test_ep_graph_gpu.py runs it over
+    several processes)."""
     if not KVM_RUN.exists():
         pytest.fail("kvm_run is not built")
     T, H, E = 64, 128, 8
@@ -152,4 +153,4 @@ def test_expert_parallel_graph_ops_fail_loudly(cuda, tmp_path):
   }}
 }}""")
     r = subprocess.run([str(KVM_RUN), str(g)], capture_output=True, text=True, timeout=120)
-    assert r.returncode == 1 and "expert parallelism" in r.stderr, r.stderr
+    assert r.returncode == 1 and "needs a communicator" in r.stderr, r.stderr

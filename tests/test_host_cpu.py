@@ -35,6 +35,7 @@ def test_reference_tests_pass_on_sm100_device(host_bin, name):
 @pytest.mark.parametrize("graph,ops,fusions", [
     ("matmul_1024", 4, []),
     ("moe_layer", 37, ["silu_gate", "router"]),
+    ("moe_layer_ep8", 37, ["silu_gate", "router"]),
     ("mlp_block", 54, ["rmsnorm", "silu_gate"])])
 def test_config_graphs_lower(host_bin, graph, ops, fusions):
     r = subprocess.run([str(host_bin / "kvm_run"), str(GRAPHS / f"{graph}.kvm"),
