@@ -223,10 +223,10 @@ def cpu_job(name, args, kw, units, unit, sample, max_reps, min_s=3.0):
 # capture, with where the figure comes from (the summary file under profiles/
 # gives the command that produced it).
 GATE_UP_TRAFFIC = {
-    "bytes": 1684342784.0,
+    "bytes": 1688299008.0,
     "src": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one gemm_pair_kernel<2> "
-           "launch on the T2048_E16 profiling case, scaled x4 to T8192_E64 (weights and "
-           "token rows both scale by 4): profiles/moe_pair_gemm_T8192.md",
+           "launch of this workload at full size (one-pass capture): "
+           "profiles/moe_layer_kernels_T8192.md",
 }
 
 
