@@ -3,7 +3,6 @@ each rank's local compute. Every output row depends only on its own token and
 the expert weights, so the sharded layer must equal the single-process oracle
 layer on the concatenated tokens bit for bit."""
 import os
-import socket
 import tempfile
 
 import numpy as np
@@ -64,10 +63,10 @@ class OracleCompute:
         return _i16(oracle.moe_combine(yb, self.pos, self.w))
 
 
-def _worker(rank, world, port, outdir):
-    os.environ["MASTER_ADDR"] = "127.0.0.1"
-    os.environ["MASTER_PORT"] = str(port)
-    dist.init_process_group("gloo", rank=rank, world_size=world)
+def _worker(rank, world, outdir):
+    # file rendezvous in the test's own directory: no port to race for
+    dist.init_process_group("gloo", init_method=f"file://{outdir}/rendezvous", rank=rank,
+                            world_size=world)
     try:
         wr, w13, w2 = _weights()
         epr = E // world
@@ -82,17 +81,11 @@ def _worker(rank, world, port, outdir):
         dist.destroy_process_group()
 
 
-def _free_port():
-    with socket.socket() as s:
-        s.bind(("127.0.0.1", 0))
-        return s.getsockname()[1]
-
-
 @pytest.mark.parametrize("world", [2, 4])
 def test_expert_parallel_matches_single_process(world):
     wr, w13, w2 = _weights()
     with tempfile.TemporaryDirectory() as d:
-        mp.start_processes(_worker, args=(world, _free_port(), d), nprocs=world,
+        mp.start_processes(_worker, args=(world, d), nprocs=world,
                            start_method="spawn")
         outs = [np.load(os.path.join(d, f"out{r}.npy")).view(np.uint16)
                 for r in range(world)]

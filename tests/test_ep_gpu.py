@@ -4,7 +4,6 @@ its experts, and the tcgen05 GEMM's per-row arithmetic does not depend on
 which rows share a tile, so the results must agree bit for bit. Skipped when
 fewer than 2 GPUs are visible."""
 import os
-import socket
 import tempfile
 
 import numpy as np
@@ -32,16 +31,16 @@ def _tokens(rank, dev):
     return torch.randn((T, H), generator=g, device=dev).to(torch.bfloat16)
 
 
-def _worker(rank, world, port, outdir, overlap=True):
+def _worker(rank, world, outdir, overlap=True):
     import torch.distributed as dist
     from kvm_b200.ep import ExpertParallelMoE
     from kvm_b200 import ops
-    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     torch.cuda.set_device(rank)
     dev = torch.device("cuda", rank)
     from datetime import timedelta
-    dist.init_process_group("nccl", rank=rank, world_size=world,
-                            timeout=timedelta(seconds=60), device_id=dev)
+    # file rendezvous in the test's own directory: no port to race for
+    dist.init_process_group("nccl", init_method=f"file://{outdir}/rendezvous", rank=rank,
+                            world_size=world, timeout=timedelta(seconds=60), device_id=dev)
     try:
         wr, w13, w2 = _make(dev)
         layer = ExpertParallelMoE(wr, w13, w2, top_k=K, max_tokens=T, rank=rank, world=world,
@@ -55,11 +54,6 @@ def _worker(rank, world, port, outdir, overlap=True):
         dist.destroy_process_group()
 
 
-def _port():
-    with socket.socket() as s:
-        s.bind(("127.0.0.1", 0))
-        return s.getsockname()[1]
-
 
 @pytest.mark.parametrize("overlap", [True, False])
 @pytest.mark.parametrize("world", [2, 4, 8])
@@ -67,7 +61,7 @@ def test_expert_parallel_matches_single_gpu(world, overlap):
     if torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
     with tempfile.TemporaryDirectory() as d:
-        mp.start_processes(_worker, args=(world, _port(), d, overlap), nprocs=world,
+        mp.start_processes(_worker, args=(world, d, overlap), nprocs=world,
                            start_method="spawn")
         outs = [torch.load(os.path.join(d, f"out{r}.pt")) for r in range(world)]
     from kvm_b200.moe import MoELayer

@@ -2,7 +2,6 @@
 and 2+ GPUs (column/row-parallel shards with NCCL all-reduce) against one GPU.
 bf16 tolerance: relative L2 <= 1e-2."""
 import os
-import socket
 import tempfile
 
 import numpy as np
@@ -62,14 +61,15 @@ def test_decoder_layer_single_gpu(cuda):
     assert rel_err(oracle.bf16_to_f32(to_bits(out)), oracle.bf16_to_f32(ref)) < 1e-2
 
 
-def _worker(rank, world, port, outdir, hq, hkv):
+def _worker(rank, world, outdir, hq, hkv):
     import torch.distributed as dist
     from datetime import timedelta
-    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    os.environ.update(NCCL_NVLS_ENABLE="0")
     torch.cuda.set_device(rank)
     dev = torch.device("cuda", rank)
-    dist.init_process_group("nccl", rank=rank, world_size=world,
-                            timeout=timedelta(seconds=60), device_id=dev)
+    # file rendezvous in the test's own directory: no port to race for
+    dist.init_process_group("nccl", init_method=f"file://{outdir}/rendezvous", rank=rank,
+                            world_size=world, timeout=timedelta(seconds=60), device_id=dev)
     try:
         w, x = _full(hq=hq, hkv=hkv)
         out = _layer(w, dev, rank, world, hq, hkv)(from_bits(x, dev))
@@ -79,11 +79,6 @@ def _worker(rank, world, port, outdir, hq, hkv):
         dist.destroy_process_group()
 
 
-def _port():
-    with socket.socket() as s:
-        s.bind(("127.0.0.1", 0))
-        return s.getsockname()[1]
-
 
 @pytest.mark.parametrize("world,hq,hkv", [(2, 4, 2), (4, 8, 4), (8, 16, 8)])
 def test_decoder_layer_tensor_parallel(world, hq, hkv):
@@ -92,7 +87,7 @@ def test_decoder_layer_tensor_parallel(world, hq, hkv):
         pytest.skip(f"needs {world} GPUs")
     w, x = _full(hq=hq, hkv=hkv)
     with tempfile.TemporaryDirectory() as d:
-        mp.start_processes(_worker, args=(world, _port(), d, hq, hkv), nprocs=world,
+        mp.start_processes(_worker, args=(world, d, hq, hkv), nprocs=world,
                            start_method="spawn")
         outs = [np.load(os.path.join(d, f"out{r}.npy")) for r in range(world)]
     assert all(np.array_equal(outs[0], o) for o in outs[1:])   # all-reduce: same on all
