@@ -306,6 +306,31 @@ def ep_parity(layer, x, wr, w13, w2, rank, world, n=256):
     return {"bitexact": bool(same), "tokens_checked": n * world, "max_abs_diff": diff}
 
 
+def graph_leg(args):
+    """The same layer as a .kvm program through the drop-in path: the
+    reference's parser and kernel->task transform with the sm_100a Device
+    target, then the executor's launches (kvm_run, one process, its own
+    seeded inputs of the graph's shapes), timed with CUDA events over
+    args.steps runs. None when the host side is not built or the workload is
+    a profiling case."""
+    exe = ROOT / "kvm_b200" / "_build" / "host" / "kvm_run"
+    g = ROOT / "kvm_b200" / "graphs" / "moe_layer.kvm"
+    if not exe.exists() or TOKENS != 8192 or EXPERTS != 64:
+        return None
+    r = subprocess.run([str(exe), str(g), "--warmup", str(max(args.warmup, 3)),
+                        "--iters", str(args.steps)], capture_output=True, text=True,
+                       timeout=600)
+    if r.returncode != 0:
+        return {"error": (r.stderr or "").strip()[-300:]}
+    d = json.loads(r.stdout.strip().splitlines()[-1])
+    ms = d["ms_per_run"]
+    return {"graph": "kvm_b200/graphs/moe_layer.kvm", "ms_per_run": ms,
+            "tokens_per_s": TOKENS / (ms / 1e3), "launches_per_run": d["launch_steps"],
+            "steps": d["steps"], "runs": d["iters"],
+            "path": ".kvm text -> reference parser -> reference kernel->task transform "
+                    "(sm_100a Device target) -> executor -> C ABI kernels"}
+
+
 def run_ours(args) -> int:
     import torch
     import torch.distributed as dist
@@ -438,6 +463,7 @@ def run_ours(args) -> int:
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline_leg(x, layer.w_router, layer.w13, layer.w2)
+    graph = graph_leg(args) if rank == 0 and world == 1 else None
 
     if rank == 0:
         line = {
@@ -467,6 +493,8 @@ def run_ours(args) -> int:
         if parity is not None:
             line["ep_bitexact"] = parity["bitexact"]
             line["ep_parity"] = parity
+        if graph is not None:
+            line["kvm_graph"] = graph
         print(json.dumps(line), flush=True)
     if world > 1:
         layer.close()
