@@ -334,6 +334,46 @@ int launch_router(const CUtensorMap& tx, const CUtensorMap& tw, const RouterPara
   return KVM_OK;
 }
 
+cudaLaunchConfig_t router_pair_config(int pairs, cudaStream_t st, cudaLaunchAttribute* attr) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(2 * pairs);
+  cfg.blockDim = dim3(kRouterPairThreads);
+  cfg.dynamicSmemBytes = RouterPairCfg::kSmem;
+  cfg.stream = st;
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cfg;
+}
+
+// SM pairs on which the pair router can be resident (cached per device).
+int router_pairs(const DeviceInfo* d, int* out) {
+  static std::mutex mu;
+  static int cached[64] = {0};
+  int dev = 0;
+  KVM_CUDA_TRY(cudaGetDevice(&dev));
+  std::lock_guard<std::mutex> lock(mu);
+  if (dev >= 0 && dev < 64 && cached[dev] > 0) {
+    *out = cached[dev];
+    return KVM_OK;
+  }
+  KVM_CUDA_TRY(cudaFuncSetAttribute(router_pair_kernel,
+                                    cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    int(RouterPairCfg::kSmem)));
+  cudaLaunchAttribute attr[1];
+  cudaLaunchConfig_t cfg = router_pair_config(d->sm_count / 2, nullptr, attr);
+  int n = 0;
+  KVM_CUDA_TRY(cudaOccupancyMaxActiveClusters(&n, router_pair_kernel, &cfg));
+  if (n <= 0) return fail(KVM_ERR_UNSUPPORTED, "router: no SM pair can be resident");
+  if (n > d->sm_count / 2) n = d->sm_count / 2;
+  if (dev >= 0 && dev < 64) cached[dev] = n;
+  *out = n;
+  return KVM_OK;
+}
+
 }  // namespace
 }  // namespace kvm
 
@@ -358,9 +398,12 @@ extern "C" int kvm_sm100_moe_router_topk(const void* x, const void* Wr,
   p.T = T; p.E = E; p.K = H; p.top_k = k;
   p.logits = logits; p.topk_idx = topk_idx; p.topk_w = topk_w;
   p.status = dev->status;
-  // Rows per tile: enough tiles to give every SM one (8192 tokens on 148
-  // SMs: 147 tiles of 56 rows), at least 32 rows and at most 128.
-  int tr = (cdiv(T, dev->sm_count) + 7) & ~7;
+  // Rows per tile: enough tiles to give every SM (E > 64) or SM pair (E <= 64)
+  // one (8192 tokens: 147 tiles of 56 rows, or 74 pair tiles of 112), at
+  // least 32 rows and at most 128.
+  int pairs = 0;
+  if (BN == 64) KVM_TRY(router_pairs(dev, &pairs));
+  int tr = (cdiv(T, BN == 64 ? pairs : dev->sm_count) + 7) & ~7;
   tr = tr < 32 ? 32 : tr > 128 ? 128 : tr;
   p.tile_rows = tr;
   const int tiles = cdiv(T, tr);
@@ -373,7 +416,16 @@ extern "C" int kvm_sm100_moe_router_topk(const void* x, const void* Wr,
                          CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
                          CU_TENSOR_MAP_SWIZZLE_128B));
   const cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (BN == 64) return launch_router<64>(tx, tw, p, grid, st);
+  if (BN == 64) {
+    KVM_CUDA_TRY(cudaFuncSetAttribute(router_pair_kernel,
+                                      cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      int(RouterPairCfg::kSmem)));
+    cudaLaunchAttribute attr[1];
+    const cudaLaunchConfig_t cfg =
+        router_pair_config(tiles < pairs ? tiles : pairs, st, attr);
+    KVM_CUDA_TRY(cudaLaunchKernelEx(&cfg, router_pair_kernel, tx, tw, p));
+    return KVM_OK;
+  }
   if (BN == 128) return launch_router<128>(tx, tw, p, grid, st);
   return launch_router<256>(tx, tw, p, grid, st);
 }
