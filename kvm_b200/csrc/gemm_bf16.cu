@@ -82,13 +82,17 @@ int launch_pair(const PairMaps& maps, const PairParams& p, long long max_tiles,
   cfg.blockDim = dim3(pair_threads(EP));
   cfg.dynamicSmemBytes = gemm_pair_smem_bytes();
   cfg.stream = st;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 2;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  // programmatic dependent launch for the single-GPU forms: the prologue
+  // (barriers, TMEM, tensor maps) overlaps the previous kernel's tail
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = EP == kEpNone ? 2 : 1;
   KVM_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, maps, p, ep));
   return KVM_OK;
 }
@@ -334,7 +338,10 @@ int launch_router(const CUtensorMap& tx, const CUtensorMap& tw, const RouterPara
   return KVM_OK;
 }
 
-cudaLaunchConfig_t router_pair_config(int pairs, cudaStream_t st, cudaLaunchAttribute* attr) {
+// Launch configuration of the pair router: clusters of 2 and (`pdl`)
+// programmatic dependent launch; `attr` must hold 2 entries.
+cudaLaunchConfig_t router_pair_config(int pairs, cudaStream_t st, cudaLaunchAttribute* attr,
+                                      bool pdl) {
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(2 * pairs);
   cfg.blockDim = dim3(kRouterPairThreads);
@@ -344,8 +351,10 @@ cudaLaunchConfig_t router_pair_config(int pairs, cudaStream_t st, cudaLaunchAttr
   attr[0].val.clusterDim.x = 2;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = pdl ? 2 : 1;
   return cfg;
 }
 
@@ -363,8 +372,8 @@ int router_pairs(const DeviceInfo* d, int* out) {
   KVM_CUDA_TRY(cudaFuncSetAttribute(router_pair_kernel,
                                     cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     int(RouterPairCfg::kSmem)));
-  cudaLaunchAttribute attr[1];
-  cudaLaunchConfig_t cfg = router_pair_config(d->sm_count / 2, nullptr, attr);
+  cudaLaunchAttribute attr[2];
+  cudaLaunchConfig_t cfg = router_pair_config(d->sm_count / 2, nullptr, attr, false);
   int n = 0;
   KVM_CUDA_TRY(cudaOccupancyMaxActiveClusters(&n, router_pair_kernel, &cfg));
   if (n <= 0) return fail(KVM_ERR_UNSUPPORTED, "router: no SM pair can be resident");
@@ -420,9 +429,9 @@ extern "C" int kvm_sm100_moe_router_topk(const void* x, const void* Wr,
     KVM_CUDA_TRY(cudaFuncSetAttribute(router_pair_kernel,
                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
                                       int(RouterPairCfg::kSmem)));
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     const cudaLaunchConfig_t cfg =
-        router_pair_config(tiles < pairs ? tiles : pairs, st, attr);
+        router_pair_config(tiles < pairs ? tiles : pairs, st, attr, true);
     KVM_CUDA_TRY(cudaLaunchKernelEx(&cfg, router_pair_kernel, tx, tw, p));
     return KVM_OK;
   }

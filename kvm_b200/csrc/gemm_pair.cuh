@@ -287,8 +287,35 @@ __global__ void __launch_bounds__(pair_threads(EP), 1)
   const int m_tiles = (p.N + 255) / 256;
   const int k_blocks = (p.K + BK - 1) / BK;
 
-  // ---- setup: tile table (identical in both CTAs), barriers, TMEM
-  if (threadIdx.x == 0) *abort_flag = 0;
+  // ---- setup: barriers, TMEM, tensor maps (no global memory: with
+  // programmatic dependent launch this overlaps the previous kernel), then
+  // the tile table (identical in both CTAs) from the group offsets
+  if (threadIdx.x == 0) {
+    *abort_flag = 0;
+    for (int s = 0; s < kPairStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 2 * kPairEpiWarps);
+      mbar_init(&ufull[a], 64);
+      mbar_init(&ufree[a], 64);
+    }
+    mbar_init(drain, 1);
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&maps.w);
+#pragma unroll
+    for (int i = 0; i < 5; ++i) tma_prefetch_desc(&maps.x[i]);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_slot, kPairTmemCols);
+    tmem_relinquish_pair();
+  }
+  pdl_trigger();
+  pdl_wait();
   for (int i = threadIdx.x; i <= G; i += blockDim.x) {
     g_off[i] = p.offsets ? p.offsets[i] : (i == 0 ? 0 : p.rows);
     if (EP == kEpDispatchGateUp && i < G) g_tme[i] = ep.tile_first[i];
@@ -320,27 +347,6 @@ __global__ void __launch_bounds__(pair_threads(EP), 1)
     // wrapping around.
     for (int g = 0; g < G; ++g)
       g_tme[g] = EP == kEpDispatchGateUp ? min(max(g_tme[g], 0), max(g_tt[g] - 1, 0)) : 0;
-    for (int s = 0; s < kPairStages; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&empty[s], 1);
-    }
-    for (int a = 0; a < 2; ++a) {
-      mbar_init(&tfull[a], 1);
-      mbar_init(&tempty[a], 2 * kPairEpiWarps);
-      mbar_init(&ufull[a], 64);
-      mbar_init(&ufree[a], 64);
-    }
-    mbar_init(drain, 1);
-    fence_mbar_init();
-  }
-  if (warp == 0 && lane == 0) {
-    tma_prefetch_desc(&maps.w);
-#pragma unroll
-    for (int i = 0; i < 5; ++i) tma_prefetch_desc(&maps.x[i]);
-  }
-  if (warp == 1) {
-    tmem_alloc_pair(tmem_slot, kPairTmemCols);
-    tmem_relinquish_pair();
   }
   tc_fence_before();
   __syncthreads();

@@ -24,6 +24,8 @@ constexpr int kMaxExperts = 1024;
 __global__ void __launch_bounds__(kPermChunk)
     permute_count_kernel(const int* __restrict__ idx, int n, int E,
                          int* __restrict__ counts, int* status) {
+  pdl_trigger();
+  pdl_wait();
   extern __shared__ int hist[];
   for (int e = threadIdx.x; e < E; e += blockDim.x) hist[e] = 0;
   __syncthreads();
@@ -45,6 +47,8 @@ __global__ void __launch_bounds__(kPermChunk)
 __global__ void permute_scan_kernel(const int* __restrict__ counts,
                                     int n_chunks, int E, int* __restrict__ base,
                                     int* __restrict__ offsets) {
+  pdl_trigger();
+  pdl_wait();
   extern __shared__ int tot[];
   const int e = threadIdx.x;
   int run = 0;
@@ -87,6 +91,8 @@ __global__ void __launch_bounds__(kPermChunk)
                         const int* __restrict__ base, int* __restrict__ pos,
                         int* __restrict__ src_token, int n_chunks,
                         int* __restrict__ offsets) {
+  pdl_trigger();
+  pdl_wait();
   constexpr int kWarps = kPermChunk / 32;
   // [kWarps][E], then (FUSED) cbase [E], tot [E], two [max(kPermChunk, E)]
   extern __shared__ int wcount[];
@@ -184,6 +190,8 @@ __global__ void __launch_bounds__(kRowThreads)
     scatter_rows_kernel(const uint4* __restrict__ x, const int* __restrict__ pos,
                         uint4* __restrict__ xp, int T, int k, int row_vecs,
                         long long n_rows_out, int* status) {
+  pdl_trigger();
+  pdl_wait();
   const int t0 = blockIdx.x * kScatterTok;
   uint4 val[kScatterTok][VPT];
 #pragma unroll
@@ -241,6 +249,8 @@ __global__ void __launch_bounds__(kRowThreads)
     combine_kernel(const uint4* __restrict__ Y, const int* __restrict__ pos,
                    const float* __restrict__ w, uint4* __restrict__ out, int T, int k,
                    int row_vecs, long long n_rows_y, int* status) {
+  pdl_trigger();
+  pdl_wait();
   const int t0 = blockIdx.x * kCombineTok;
   int src[kCombineTok][8];
   float wt[kCombineTok][8];
@@ -304,12 +314,13 @@ int n_chunks_of(int T, int k) {
 // The permutation's launches: histogram, then either the scans as their own
 // single-block pass and the ranks, or (small count matrices) the ranks with
 // the scans folded in.
+// `pdl`: launch with programmatic dependent launch (the workspace entry point;
+// the allocation-free one launches plainly).
 int launch_permute(const int32_t* topk_idx, int n, int k, int E, int nc, int* counts,
                    int* base, int32_t* expert_offsets, int32_t* pos, int32_t* src_token,
-                   int* status, cudaStream_t st) {
-  permute_count_kernel<<<nc, kPermChunk, E * sizeof(int), st>>>(topk_idx, n, E, counts,
-                                                                 status);
-  KVM_CUDA_TRY(cudaGetLastError());
+                   int* status, cudaStream_t st, bool pdl) {
+  KVM_CUDA_TRY(launch_ex(pdl, permute_count_kernel, dim3(nc), dim3(kPermChunk),
+                         E * sizeof(int), st, topk_idx, n, E, counts, status));
   const size_t rank_smem = (kPermChunk / 32) * E * sizeof(int);
   if (static_cast<long long>(nc) * E <= 16 * 1024) {
     const size_t smem =
@@ -318,21 +329,22 @@ int launch_permute(const int32_t* topk_idx, int n, int k, int E, int nc, int* co
       KVM_CUDA_TRY(cudaFuncSetAttribute(permute_rank_kernel<true>,
                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
                                         int(smem)));
-    permute_rank_kernel<true><<<nc, kPermChunk, smem, st>>>(
-        topk_idx, n, k, E, counts, pos, src_token, nc, expert_offsets);
-    KVM_CUDA_TRY(cudaGetLastError());
+    KVM_CUDA_TRY(launch_ex(pdl, permute_rank_kernel<true>, dim3(nc), dim3(kPermChunk), smem,
+                           st, topk_idx, n, k, E, static_cast<const int*>(counts), pos,
+                           src_token, nc, expert_offsets));
     return KVM_OK;
   }
   const int scan_threads = ((E + 31) / 32) * 32;
-  permute_scan_kernel<<<1, scan_threads, E * sizeof(int), st>>>(counts, nc, E, base,
-                                                                 expert_offsets);
-  KVM_CUDA_TRY(cudaGetLastError());
+  KVM_CUDA_TRY(launch_ex(pdl, permute_scan_kernel, dim3(1), dim3(scan_threads),
+                         E * sizeof(int), st, static_cast<const int*>(counts), nc, E, base,
+                         expert_offsets));
   if (rank_smem > 48 * 1024)
     KVM_CUDA_TRY(cudaFuncSetAttribute(permute_rank_kernel<false>,
                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
                                       int(rank_smem)));
-  permute_rank_kernel<false><<<nc, kPermChunk, rank_smem, st>>>(
-      topk_idx, n, k, E, base, pos, src_token, nc, expert_offsets);
+  KVM_CUDA_TRY(launch_ex(pdl, permute_rank_kernel<false>, dim3(nc), dim3(kPermChunk),
+                         rank_smem, st, topk_idx, n, k, E, static_cast<const int*>(base), pos,
+                         src_token, nc, expert_offsets));
   KVM_CUDA_TRY(cudaGetLastError());
   return KVM_OK;
 }
@@ -368,7 +380,7 @@ extern "C" int kvm_sm100_moe_permute(const int32_t* topk_idx, int T, int k,
   int* counts = static_cast<int*>(workspace);
   int* base = counts + static_cast<long long>(nc) * E;
   return launch_permute(topk_idx, n, k, E, nc, counts, base, expert_offsets, pos, src_token,
-                        dev->status, st);
+                        dev->status, st, true);
 }
 
 extern "C" int kvm_sm100_moe_scatter_rows(const void* x, const int32_t* pos,
@@ -389,11 +401,11 @@ extern "C" int kvm_sm100_moe_scatter_rows(const void* x, const int32_t* pos,
   const uint4* xv = static_cast<const uint4*>(x);
   uint4* xpv = static_cast<uint4*>(xp);
   if (row_vecs <= kRowThreads)
-    scatter_rows_kernel<1><<<blocks, kRowThreads, 0, st>>>(xv, pos, xpv, T, k, row_vecs, n_out, dev->status);
+    KVM_CUDA_TRY(launch_ex(true, scatter_rows_kernel<1>, dim3(blocks), dim3(kRowThreads), 0, st, xv, pos, xpv, T, k, row_vecs, n_out, dev->status));
   else if (row_vecs <= 2 * kRowThreads)
-    scatter_rows_kernel<2><<<blocks, kRowThreads, 0, st>>>(xv, pos, xpv, T, k, row_vecs, n_out, dev->status);
+    KVM_CUDA_TRY(launch_ex(true, scatter_rows_kernel<2>, dim3(blocks), dim3(kRowThreads), 0, st, xv, pos, xpv, T, k, row_vecs, n_out, dev->status));
   else if (row_vecs <= 4 * kRowThreads)
-    scatter_rows_kernel<4><<<blocks, kRowThreads, 0, st>>>(xv, pos, xpv, T, k, row_vecs, n_out, dev->status);
+    KVM_CUDA_TRY(launch_ex(true, scatter_rows_kernel<4>, dim3(blocks), dim3(kRowThreads), 0, st, xv, pos, xpv, T, k, row_vecs, n_out, dev->status));
   else
     return fail(KVM_ERR_UNSUPPORTED, "moe_scatter_rows: rows wider than 8192 elements");
   KVM_CUDA_TRY(cudaGetLastError());
@@ -417,11 +429,11 @@ extern "C" int kvm_sm100_moe_combine(const void* Y, const int32_t* pos,
   const uint4* yv = static_cast<const uint4*>(Y);
   uint4* ov = static_cast<uint4*>(out);
   if (row_vecs <= kRowThreads)
-    combine_kernel<1><<<blocks, kRowThreads, 0, st>>>(yv, pos, w, ov, T, k, row_vecs, n_y, dev->status);
+    KVM_CUDA_TRY(launch_ex(true, combine_kernel<1>, dim3(blocks), dim3(kRowThreads), 0, st, yv, pos, w, ov, T, k, row_vecs, n_y, dev->status));
   else if (row_vecs <= 2 * kRowThreads)
-    combine_kernel<2><<<blocks, kRowThreads, 0, st>>>(yv, pos, w, ov, T, k, row_vecs, n_y, dev->status);
+    KVM_CUDA_TRY(launch_ex(true, combine_kernel<2>, dim3(blocks), dim3(kRowThreads), 0, st, yv, pos, w, ov, T, k, row_vecs, n_y, dev->status));
   else if (row_vecs <= 4 * kRowThreads)
-    combine_kernel<4><<<blocks, kRowThreads, 0, st>>>(yv, pos, w, ov, T, k, row_vecs, n_y, dev->status);
+    KVM_CUDA_TRY(launch_ex(true, combine_kernel<4>, dim3(blocks), dim3(kRowThreads), 0, st, yv, pos, w, ov, T, k, row_vecs, n_y, dev->status));
   else
     return fail(KVM_ERR_UNSUPPORTED, "moe_combine: rows wider than 8192 elements");
   KVM_CUDA_TRY(cudaGetLastError());
@@ -526,5 +538,5 @@ extern "C" int kvm_sm100_moe_permute_noalloc(const int32_t* topk_idx, int T,
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const int n = T * k;
   return launch_permute(topk_idx, n, k, E, static_cast<int>(nc), counts, base, expert_offsets,
-                        pos, src_token, status, st);
+                        pos, src_token, status, st, false);
 }

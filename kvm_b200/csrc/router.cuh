@@ -29,6 +29,7 @@
 #include <cuda_bf16.h>
 
 #include "ptx.cuh"
+#include "runtime.h"
 
 namespace kvm {
 
@@ -490,6 +491,9 @@ __global__ void __launch_bounds__(kRouterPairThreads, 1)
   cluster_sync_all();   // the other CTA's barriers are initialised before any remote arrive
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // x may still be written, and the outputs read, by the previous kernel
+  pdl_trigger();
+  pdl_wait();
 
   if (warp == 0) {
     if (lane == 0) {

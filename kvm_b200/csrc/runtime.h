@@ -28,6 +28,38 @@ struct DeviceInfo {
 // last error set) if the device cannot be queried.
 const DeviceInfo* device_info();
 
+// Launch `kern` on `st`; with `pdl`, programmatic dependent launch is
+// allowed: the kernel may start (and run its prologue) while the previous
+// kernel of the stream is finishing. Every kernel launched that way calls
+// pdl_wait() (below) before it touches global memory that an earlier kernel
+// of the stream writes or reads.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_ex(bool pdl, void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                      cudaStream_t st, Args&&... args) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kern, static_cast<Args&&>(args)...);
+}
+
+// Device side of programmatic dependent launch. pdl_wait(): block until the
+// kernels this one may overlap have completed and their memory is visible.
+// pdl_trigger(): let the next kernel of the stream start launching. Both do
+// nothing in a kernel launched without the attribute.
+#ifdef __CUDACC__
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+#endif
+
 // Record `msg` as this thread's last error and return `code`.
 int fail(int code, const std::string& msg);
 int fail_cuda(cudaError_t e, const char* what);
