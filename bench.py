@@ -223,7 +223,7 @@ def cpu_job(name, args, kw, units, unit, sample, max_reps, min_s=3.0):
 # capture, with where the figure comes from (the summary file under profiles/
 # gives the command that produced it).
 GATE_UP_TRAFFIC = {
-    "bytes": 1688299008.0,
+    "bytes": 1808847360.0,
     "src": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one gemm_pair_kernel<2> "
            "launch of this workload at full size (one-pass capture): "
            "profiles/moe_layer_kernels_T8192.md",
