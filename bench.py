@@ -401,7 +401,11 @@ def run_ours(args) -> int:
     ms = ev0.elapsed_time(ev1)
     # per-launch times in a second pass of the same steps: events between the
     # launches would serialise them (no programmatic dependent launch), so the
-    # timed loop above records none
+    # timed loop above records none. The ranks start it together (stopping the
+    # clock sampler takes a different time on each), else the first exchange
+    # of the pass would absorb the difference.
+    barrier()
+    torch.cuda.synchronize()
     for i in range(args.steps):
         layer(x, probe=probe.next_call())
     torch.cuda.synchronize()
@@ -426,7 +430,9 @@ def run_ours(args) -> int:
     x_host = [x.cpu().pin_memory() for _ in range(2)]
     out_host = [torch.empty((TOKENS, HIDDEN), dtype=torch.bfloat16).pin_memory()
                 for _ in range(2)]
-    e2e_steps = max(3, min(args.steps, 50))
+    # at least 50 steps, so that filling and draining the three-stream
+    # pipeline (one step's copy in, compute, copy out) is a small part
+    e2e_steps = min(max(args.steps, 50), 200)
     for i in range(3):
         pipe.submit(x_host[i % 2], out_host[i % 2])
     pipe.synchronize()
