@@ -358,10 +358,11 @@ __global__ void __launch_bounds__(kRouterThreads, 1)
 // one token tile and each walks half of K, and the epilogue spreads a row over
 // 4 threads. Measured on B200 (8192 tokens, H 4096, E 64; 50 launches queued
 // behind a sleep kernel): 23.4 us per launch against 25.9 us for the one-SM
-// kernel. Launched right after a kernel that leaves 256 MB of written lines
-// in L2, both take 30.7 us, which is what the router costs inside the MoE
-// layer (after the combine's writes): consistent with the reads of x waiting
-// for L2 to write those lines back to HBM.
+// kernel (20.7 us once launched with programmatic dependent launch, which
+// overlaps one launch's prologue with the previous one's tail). Right after
+// another kernel: 26.7 us after a 256 MB read, 30.7 us after a 256 MB copy
+// (written lines that L2 writes back while x streams in) -- the latter is
+// what it costs inside the MoE layer, after the combine's writes.
 //
 //   warp 0 (one lane)  TMA producer for this CTA's K half
 //   warp 1 (one lane)  MMA issuer: M = 128 (the tile's rows), N = 64
