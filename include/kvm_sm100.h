@@ -102,13 +102,24 @@ int kvm_sm100_transpose_bf16(const void* in, void* out, int G, int R, int C,
 
 /* ---------------------------------------------------------------- MoE --- */
 
+/* The router, permute (workspace form), scatter, grouped GEMMs and combine
+ * below launch with programmatic dependent launch: a launch may start its
+ * prologue while the previous kernel on the stream finishes, and touches
+ * global memory only after that kernel has completed. Stream order is kept
+ * as for any launch. */
+
 /* Router GEMM fused with softmax and top-k. logits[T,E] = x[T,H] . Wr^T
  * (Wr stored [E, H]); probabilities p = softmax(logits) in fp32; topk_idx
  * [T,k] are the k largest logits per token (ties: lower expert index first,
  * descending order), topk_w [T,k] their probabilities (no renormalisation).
  * 1 <= E <= 256 in this build (E > 256: KVM_ERR_UNSUPPORTED); 1 <= k <= min(8, E).
- * A token's logits are the same bits in any batch: one accumulator, K always
- * in the same order, whichever tile or CTA computes the row.
+ * A token's logits are the same bits in any batch: for E <= 64 the two halves
+ * of K are accumulated separately (the split depends only on H) and added in
+ * a fixed order; for E > 64 one accumulator walks K in order. A NaN logit
+ * ranks below every number in the top-k (E <= 64).
+ * The launch may overlap the tail of the previous kernel on the stream
+ * (programmatic dependent launch); it reads x and writes its outputs only
+ * after that kernel has completed.
  * Replaces the routing half of kernel.comm.moe_dispatch
  * (src/ir/dialect/kernel/dialect.cpp:65, passed through to
  * task.comm.moe_dispatch by src/device/device.cpp:143-147). */
