@@ -16,7 +16,8 @@
 // the same bits whichever tile, CTA or batch computes them: one accumulator,
 // K always in the same order.
 //
-// Measured on B200 with this kernel at E = 64 (8192 tokens, H 4096), per
+// Measured on B200 with this kernel at E = 64 (8192 tokens, H 4096; it ran
+// E <= 64 too before router_pair_kernel), per
 // launch, timed as 50 launches queued behind a sleep kernel: 28.0 us in all
 // (25.9 us once mbarrier waits carry a suspend-time hint, ptx.cuh);
 // 8.3 us with no K block at all (2.4 us of it launch and setup, the rest the
@@ -52,7 +53,7 @@ struct RouterParams {
 // or past TR read the following bytes (their results land in TMEM lanes that
 // are never read), and a pad after the last stage keeps those reads inside
 // the allocation. Barriers live in static shared memory.
-template <int BN>
+template <int BN>   // 128 or 256 (E <= 64 runs router_pair_kernel)
 struct RouterCfg {
   static constexpr uint32_t kBBytes = BN * kRouterBK * 2;
   static constexpr int kMaxStages = 16;
@@ -235,98 +236,43 @@ __global__ void __launch_bounds__(kRouterThreads, 1)
       int n = 0;
       float mx = -INFINITY;
       float sum = 0.f;
-      if constexpr (BN == 64) {
-        // all 64 logits of the row in registers
-        float v[64];
+      // pass 1: logits, max, top-k (insertion list), 32 columns at a time
+#pragma unroll 1
+      for (int sl = 0; sl < BN / 32; ++sl) {
+        float v[32];
         {
-          uint32_t r0[32], r1[32];
-          tmem_ld32(t_row, r0);
-          tmem_ld32(t_row + 32, r1);
+          uint32_t r[32];
+          tmem_ld32(t_row + sl * 32, r);
           tmem_wait_ld();
 #pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            v[i] = __uint_as_float(r0[i]);
-            v[32 + i] = __uint_as_float(r1[i]);
-          }
-        }
-        if (row_ok) {
-          if (E == 64) {
-#pragma unroll
-            for (int i = 0; i < 16; ++i)
-              reinterpret_cast<float4*>(lrow)[i] =
-                  make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
-          } else {
-#pragma unroll
-            for (int i = 0; i < 64; ++i)
-              if (i < E) lrow[i] = v[i];
-          }
+          for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
         }
 #pragma unroll
-        for (int i = 0; i < 64; ++i)
-          if (i < E) mx = fmaxf(mx, v[i]);
-#pragma unroll
-        for (int i = 0; i < 64; ++i)
-          if (i < E) sum += expf(v[i] - mx);
-        // top-k by k selection passes over the 64 registers (the largest
-        // untaken value, ties to the lower index): far fewer instructions than
-        // an insertion list for k <= 8
-        uint64_t taken = 0;
-        for (int j = 0; j < k; ++j) {
-          float best = -INFINITY;
-          int b = -1;
-#pragma unroll
-          for (int i = 0; i < 64; ++i) {
-            const bool free_i = i < E && ((taken >> i) & 1ull) == 0;
-            if (free_i && (b < 0 || v[i] > best)) {
-              best = v[i];
-              b = i;
-            }
+        for (int i = 0; i < 32; ++i) {
+          const int e = sl * 32 + i;
+          if (e < E) {
+            if (row_ok) lrow[e] = v[i];
+            mx = fmaxf(mx, v[i]);
+            topk_insert(bv, bi, n, k, v[i], e);
           }
-          taken |= 1ull << b;
-          if (row_ok) {
-            p.topk_idx[static_cast<long long>(row) * k + j] = b;
-            p.topk_w[static_cast<long long>(row) * k + j] = expf(best - mx) / sum;
-          }
-        }
-      } else {
-        // pass 1: logits, max, top-k (insertion list), 32 columns at a time
-#pragma unroll 1
-        for (int sl = 0; sl < BN / 32; ++sl) {
-          float v[32];
-          {
-            uint32_t r[32];
-            tmem_ld32(t_row + sl * 32, r);
-            tmem_wait_ld();
-#pragma unroll
-            for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
-          }
-#pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const int e = sl * 32 + i;
-            if (e < E) {
-              if (row_ok) lrow[e] = v[i];
-              mx = fmaxf(mx, v[i]);
-              topk_insert(bv, bi, n, k, v[i], e);
-            }
-          }
-        }
-        // pass 2: softmax denominator in ascending expert order
-#pragma unroll 1
-        for (int sl = 0; sl < BN / 32; ++sl) {
-          float v[32];
-          {
-            uint32_t r[32];
-            tmem_ld32(t_row + sl * 32, r);
-            tmem_wait_ld();
-#pragma unroll
-            for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
-          }
-#pragma unroll
-          for (int i = 0; i < 32; ++i)
-            if (sl * 32 + i < E) sum += expf(v[i] - mx);
         }
       }
-      if (BN > 64 && row_ok) {
+      // pass 2: softmax denominator in ascending expert order
+#pragma unroll 1
+      for (int sl = 0; sl < BN / 32; ++sl) {
+        float v[32];
+        {
+          uint32_t r[32];
+          tmem_ld32(t_row + sl * 32, r);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+        }
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+          if (sl * 32 + i < E) sum += expf(v[i] - mx);
+      }
+      if (row_ok) {
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
           if (j < k) {
