@@ -67,6 +67,30 @@ def test_router_logits_do_not_depend_on_the_batch(cuda, H):
     assert rel_err(full.logits[:64].cpu().numpy(), ref) < 1e-5
 
 
+@pytest.mark.parametrize("T,H,E,k", [
+    # one K block: the second CTA of each SM pair has no K half (its partial
+    # is zero), and 157 tiles of 128 rows give the pairs two or three tiles
+    # each (the exchange buffers of both tile parities in use)
+    (20000, 64, 37, 3),
+    # one expert; an odd number of 64-deep K blocks (K halves of 2 and 1)
+    (333, 192, 1, 1),
+    # a partial last K block in the second half, all 8 of 64 experts taken
+    (5000, 4000, 64, 8)])
+def test_router_sm_pairs_edge_shapes(cuda, T, H, E, k):
+    """The E <= 64 router (SM pairs, K split in two) at shapes that reach its
+    corner paths, against the oracle."""
+    rng = np.random.default_rng(T + H + E)
+    x = oracle.normal_bf16(rng, (T, H))
+    wr = oracle.normal_bf16(rng, (E, H), 0.05)
+    r = ops.moe_route(from_bits(x, cuda), from_bits(wr, cuda), top_k=k)
+    ops.device_status()
+    logits = r.logits.cpu().numpy()
+    assert rel_err(logits, oracle.gemm(x, wr, b_layout="nk", out_f32=True)) < 1e-5
+    idx, w = oracle.moe_topk(logits, k)
+    assert np.array_equal(r.topk_idx.cpu().numpy(), idx)
+    np.testing.assert_allclose(r.topk_w.cpu().numpy(), w, rtol=1e-5, atol=1e-7)
+
+
 def test_router_ties_take_lower_expert(cuda):
     T, H, E = 128, 64, 64
     x = np.zeros((T, H), dtype=np.uint16)
