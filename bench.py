@@ -286,7 +286,7 @@ def ep_parity(layer, x, wr, w13, w2, rank, world, n=256):
     """Bit-exact check of the expert-parallel layer: the first n tokens of
     every rank's batch, gathered on rank 0, through the one-GPU layer (which
     holds all E experts). Every rank takes part in the gather; rank 0 returns
-    the verdict, the others None."""
+    the comparison, the others None."""
     import torch
     import torch.distributed as dist
     from kvm_b200.moe import MoELayer
